@@ -1,0 +1,210 @@
+/*
+ * pearl_b200.h -- C ABI of the B200 (sm_100a) Pearl mining kernels.
+ *
+ * Plain pointers, sizes and a CUDA stream handle; no torch types.  Every
+ * entry point is asynchronous on `stream` (a cudaStream_t passed as void*),
+ * returns PB2_OK or a PB2_ERR_* code after validating its arguments, and
+ * allocates nothing: the caller owns every input, output and scratch buffer,
+ * exactly like the reference's pybind11 / TORCH_LIBRARY operators
+ * (miner/pearl-gemm/csrc/gemm/pearl_gemm_api.cpp) whose argument lists the
+ * parameter structs below mirror.  Device pointers must be on `device`.
+ *
+ * Matrix layouts are row-major and contiguous:
+ *   A (m,k) int8, B (n,k) int8, EAL (m,r) int8, EBR (n,r) int8,
+ *   EAR_R_major / EBL_R_major (k,r) int8, EAR_K_major / EBL_K_major (r,k) int8,
+ *   *_fp16 (rows,r) IEEE half, AxEBL / EARxBpEB (rows,r) int32 or half,
+ *   A_scales (m) / B_scales (n) float, C (m,n) bfloat16.
+ */
+#ifndef PEARL_B200_H_
+#define PEARL_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define PB2_API __attribute__((visibility("default")))
+#else
+#define PB2_API
+#endif
+
+#define PB2_ABI_VERSION 1
+
+/* Status codes. */
+#define PB2_OK 0
+#define PB2_ERR_INVALID_ARGUMENT 1 /* shape / alignment / missing tensor */
+#define PB2_ERR_UNSUPPORTED_CONFIG 2 /* "No ... kernel found with given config" */
+#define PB2_ERR_CUDA 3               /* a CUDA runtime call failed */
+#define PB2_ERR_DEVICE_TIMEOUT 4     /* a bounded device-side wait ran out */
+#define PB2_ERR_NO_DRIVER_ENTRY 5    /* cuTensorMapEncodeTiled unavailable */
+
+/* Sizes of the caller-owned signalling buffers.
+ * Header: byte-compatible with the reference HostSignalHeader
+ * (miner/pearl-gemm/csrc/gemm/host_signal_header.hpp:21-50), 640 bytes.
+ * Sync: the reference HostSignalSync {int lock; int status} followed by
+ * {uint32 hit_count; int32 error}; the caller zeroes it before each call. */
+#define PB2_HOST_SIGNAL_HEADER_SIZE 640
+#define PB2_HOST_SIGNAL_SYNC_SIZE 16
+/* One entry of the optional device hit list:
+ * {row_offset, col_offset, tile_m, tile_n, digest[8]} as uint32. */
+#define PB2_HIT_WORDS 12
+
+/* Replaces get_host_signal_header_size (pearl_gemm_api.cpp:48-50). */
+PB2_API int64_t pb2_host_signal_header_size(void);
+/* Replaces get_host_signal_sync_size (pearl_gemm_api.cpp:52-54). */
+PB2_API int64_t pb2_host_signal_sync_size(void);
+/* Human-readable text for a PB2_* status code (never NULL). */
+PB2_API const char* pb2_status_string(int status);
+/* Text of the last CUDA error seen by this library on the calling thread. */
+PB2_API const char* pb2_last_cuda_error(void);
+/* ABI version of the loaded library (PB2_ABI_VERSION). */
+PB2_API int pb2_abi_version(void);
+
+/* ------------------------------------------------------------- noise_gen ---
+ * Replaces noise_gen (pearl_gemm_api.cpp:168-298; kernel
+ * noise_generation_kernel.h:88-758).  Any output may be NULL (not produced).
+ * Sparse outputs are fully written (zeros included).  key_a / key_b are
+ * 32-byte device buffers; key_a is required when any A-side output is
+ * requested, key_b for B-side outputs.  aux_buffer (aux_words uint32,
+ * aux_words % 4 == 0) is zeroed when given. */
+typedef struct pb2_noise_gen_params {
+  int device;
+  int64_t m, n, k, r;
+  int8_t* EAL;          /* (m,r)  */
+  void* EAL_fp16;       /* (m,r) half, value * kEALScaleFactorDenoise (-1) */
+  int8_t* EAR_R_major;  /* (k,r)  */
+  int8_t* EAR_K_major;  /* (r,k)  */
+  int8_t* EBL_R_major;  /* (k,r)  */
+  int8_t* EBL_K_major;  /* (r,k)  */
+  int8_t* EBR;          /* (n,r)  */
+  void* EBR_fp16;       /* (n,r) half, value * kEBRScaleFactorDenoise (-4) */
+  const uint8_t* key_a; /* 32 bytes */
+  const uint8_t* key_b; /* 32 bytes */
+  uint32_t* aux_buffer;
+  int64_t aux_words;
+} pb2_noise_gen_params;
+PB2_API int pb2_noise_gen(const pb2_noise_gen_params* p, void* stream);
+
+/* ------------------------------------------------------- noise_A / noise_B -
+ * noise_A replaces pearl_gemm_api.cpp:300-398:
+ *   ApEA = A + EAL . EAR^T                (EAR given as (k,r) R-major)
+ *   AxEBL = A . EBL^T, EBL given as (r,k) K-major; int32 exact, or half
+ *   scaled by 2^-14 when out_is_fp16.
+ * noise_B replaces pearl_gemm_api.cpp:400-500:
+ *   BpEB = B + EBR . EBL^T               (EBL given as (k,r) R-major)
+ *   EARxBpEB = BpEB . EAR^T, EAR given as (r,k) K-major; int32 or half * 2^-12.
+ * The generic form below serves both: X = A or B, EL = EAL or EBR,
+ * E_rmajor = EAR_R_major or EBL_R_major, E_kmajor = EBL_K_major or
+ * EAR_K_major.  int32 outputs are ACCUMULATED (atomic adds; zero them first,
+ * as the reference requires for its split-K path); half outputs are written.
+ * For noise_B the projection uses the noised operand XpE. */
+typedef struct pb2_noising_params {
+  int device;
+  int64_t rows, k, r;
+  const int8_t* X;        /* (rows,k) */
+  const int8_t* EL;       /* (rows,r) */
+  const int8_t* E_rmajor; /* (k,r)    */
+  const int8_t* E_kmajor; /* (r,k)    */
+  int8_t* XpE;            /* (rows,k) out */
+  void* proj;             /* (rows,r) out, int32 or half */
+  int proj_is_fp16;
+  int k_blocks_per_split; /* <0: heuristic; 0: no split; >0: k-blocks of 128 per CTA */
+} pb2_noising_params;
+PB2_API int pb2_noise_A(const pb2_noising_params* p, void* stream);
+PB2_API int pb2_noise_B(const pb2_noising_params* p, void* stream);
+
+/* ----------------------------------------------------- denoise_converter ---
+ * Replaces denoise_converter (pearl_gemm_api.cpp:114-166): int32 -> half
+ * with scale 2^-12 (EARxBpEB) and 2^-14 (AxEBL).  Either pair may be NULL. */
+typedef struct pb2_denoise_converter_params {
+  int device;
+  int64_t m, n, r;
+  const int32_t* EARxBpEB_in; /* (n,r) */
+  const int32_t* AxEBL_in;    /* (m,r) */
+  void* EARxBpEB_out;         /* (n,r) half */
+  void* AxEBL_out;            /* (m,r) half */
+} pb2_denoise_converter_params;
+PB2_API int pb2_denoise_converter(const pb2_denoise_converter_params* p, void* stream);
+
+/* ------------------------------------------------------ noisy_gemm / gemm ---
+ * Replaces noisy_gemm (pearl_gemm_api.cpp:618-936) and gemm (:502-616).
+ * The main kernel computes, per 128 x 256 output tile,
+ *   S = ApEA . BpEB^T (int32, tcgen05 int8 MMA, accumulator in TMEM),
+ * folds the protocol transcript of every 2 x 64 hash tile every r steps of k,
+ * hashes it with keyed BLAKE3 (key = pow_key) and compares with pow_target,
+ * then (unless skip_denoising)
+ *   C = bf16(A_scales[m] * B_scales[n] *
+ *            (S + EAL_fp16 . EARxBpEB_fp16^T * 2^12 + AxEBL_fp16 . EBR_fp16^T * 2^12)).
+ * run_noising_a / run_noising_b run noise_A / noise_B first (from A, EAL,
+ * EAR_R_major, EBL_K_major / B, EBR, EAR_K_major, EBL_R_major); the int32
+ * denoise factors, when given, are produced there and converted to half.
+ * Hits: the first in-bounds hit writes the pinned host header and sets
+ * sync->status (no spinning); every hit is appended to the optional device
+ * hit list.  The optional debug outputs (transcripts, digests: one slot per
+ * protocol hash tile, index (row/16*8 + row%16) * (n/64) + col/256*4 + (col%256)/2;
+ * inner_hash_counter: one count per hash-tile fold) need m % 16 == 0 and
+ * n % 256 == 0. */
+typedef struct pb2_gemm_params {
+  int device;
+  int64_t m, n, k, r;
+  /* inputs of the optional noising stage */
+  const int8_t* A;
+  const int8_t* B;
+  const int8_t* EAL;
+  const int8_t* EBR;
+  const int8_t* EAR_R_major;
+  const int8_t* EBL_R_major;
+  const int8_t* EAR_K_major;
+  const int8_t* EBL_K_major;
+  int32_t* AxEBL_int32;    /* optional */
+  int32_t* EARxBpEB_int32; /* optional */
+  /* main kernel operands */
+  int8_t* ApEA;            /* (m,k) */
+  int8_t* BpEB;            /* (n,k) */
+  const void* EAL_fp16;    /* (m,r) half */
+  const void* EBR_fp16;    /* (n,r) half */
+  void* AxEBL_fp16;        /* (m,r) half */
+  void* EARxBpEB_fp16;     /* (n,r) half */
+  const float* A_scales;   /* (m) */
+  const float* B_scales;   /* (n) */
+  void* C;                 /* (m,n) bf16 */
+  void* host_signal_header_pinned; /* PB2_HOST_SIGNAL_HEADER_SIZE bytes, host pinned */
+  void* host_signal_sync;          /* PB2_HOST_SIGNAL_SYNC_SIZE bytes, device */
+  const uint32_t* pow_target;      /* 8 words, little-endian word order */
+  const uint32_t* pow_key;         /* 8 words */
+  /* tile / schedule knobs (reference names) */
+  int tile_size_m, tile_size_n, tile_size_k;
+  int cluster_size_m, cluster_size_n;
+  int pipeline_stages; /* <= 0: default */
+  int swizzle;         /* <= 0: heuristic; raster group size in tiles */
+  int swizzle_n_maj;
+  int run_noising_a, run_noising_b;
+  int k_blocks_per_split_noising_a, k_blocks_per_split_noising_b;
+  int skip_reduction, skip_denoising;
+  /* B200 extensions (all optional) */
+  uint64_t* inner_hash_counter;
+  int enable_debug;
+  uint32_t* hits;        /* hit_capacity * PB2_HIT_WORDS words */
+  int64_t hit_capacity;
+  uint32_t* transcripts; /* (m/2)*(n/64) * 16 words */
+  uint32_t* digests;     /* (m/2)*(n/64) * 8 words  */
+} pb2_gemm_params;
+PB2_API int pb2_noisy_gemm(const pb2_gemm_params* p, void* stream);
+/* Plain scaled GEMM: C = bf16(A_scales * (A . B^T) * B_scales), reading the
+ * operands from p->ApEA / p->BpEB (the reference passes A and B there). */
+PB2_API int pb2_gemm(const pb2_gemm_params* p, void* stream);
+
+/* -------------------------------------------------------------- inner_hash -
+ * Replaces inner_hash (pearl_gemm_api.cpp:939-970, inner_hash_kernel.cu:11-58):
+ * out[0] = the XOR of in[0..n) added up `iterations` times (mod 2^32), with
+ * n in {64,96,128,192,256} and iterations in {1, 100000}. */
+PB2_API int pb2_inner_hash(int device, const uint32_t* in, int64_t n, uint32_t* out, int64_t iterations,
+                   void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PEARL_B200_H_ */

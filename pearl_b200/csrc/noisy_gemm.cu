@@ -1,0 +1,546 @@
+// noisy_gemm.cu -- the mined GEMM on sm_100a tensor cores.
+//
+// One CTA computes a 128 x 256 output tile S = ApEA . BpEB^T (int8 x int8 ->
+// int32) with tcgen05.mma; the accumulator lives in 256 TMEM columns, so two
+// CTAs share an SM and the tensor core alternates between them.  Operand tiles
+// (128 bytes of K per stage, 128-byte swizzle) stream in by TMA.
+//
+// Transcript (protocol: zk-pow/src/ffi/mine.rs:86-107; GPU twin
+// pearl-gemm/csrc/gemm/pow_utils.hpp:129-200 and collective_mainloop.hpp:270-317):
+// every R steps of K the MMA warp commits, the four epilogue warps read the
+// running accumulator from TMEM (thread = row), XOR each row's 256 values into
+// four column classes ((col / 2) % 4), pair rows r and r + 8 with one shuffle
+// and rotate-xor the result into word (chunk % 16) of the 16-word transcript of
+// each 2 x 64 protocol hash tile (rows {r, r+8} x cols {c + 8j, c + 8j + 1}).
+// Each epilogue thread owns two hash tiles.  The fold and the rotate-xor are
+// GF(2)-linear, so folding the two rows separately and XOR-ing is exact.
+//
+// Epilogue (collective_epilogue.hpp:361-599 semantics): the final int32
+// accumulator is rewritten in TMEM as f32 * 2^-12, two f16 MMAs add the
+// low-rank denoise terms EAL_fp16 . EARxBpEB_fp16^T + AxEBL_fp16 . EBR_fp16^T,
+// and C = bf16(D * 2^12 * A_scales[m] * B_scales[n]) is stored.  Each hash
+// tile's transcript is hashed with keyed BLAKE3 (pow_utils.hpp:205-234) and
+// compared with the uint256 target; hits are published without any spin
+// lock (first hit claims the pinned host header with one atomicCAS).
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <cstring>
+
+#include "pb2_common.cuh"
+
+namespace pb2 {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 128;  // bytes of K per pipeline stage (one 128-byte swizzle row)
+constexpr int kStages = 2;
+constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
+constexpr int kAStage = BM * BK;
+constexpr int kBStage = BN * BK;
+constexpr int kStageBytes = kAStage + kBStage;
+constexpr int kTmemCols = 256;
+constexpr uint32_t kIdescI8 = idesc_i8(BM, BN);
+constexpr uint32_t kIdescF16 = idesc_f16(BM, BN);
+
+struct MainArgs {
+  CUtensorMap tmA, tmB;      // ApEA (m,k), BpEB (n,k): int8
+  CUtensorMap tmDA0, tmDB0;  // EAL_fp16 (m,r), EARxBpEB_fp16 (n,r)
+  CUtensorMap tmDA1, tmDB1;  // AxEBL_fp16 (m,r), EBR_fp16 (n,r)
+  int M, N, K, R;
+  int tiles_m, tiles_n, num_tiles, group;
+  const float* sA;
+  const float* sB;
+  __nv_bfloat16* C;
+  SignalSync* sync;
+  SignalHeader* header;
+  const uint32_t* target;
+  const uint32_t* key;
+  unsigned long long* counter;
+  uint32_t* hits;
+  long long hit_cap;
+  uint32_t* transcripts;
+  uint32_t* digests;
+};
+
+struct Smem {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t acc_full;
+  uint64_t acc_empty;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__device__ __forceinline__ void tile_coords(const MainArgs& a, int t, int& tm, int& tn) {
+  const int gsize = a.group * a.tiles_n;
+  const int g = t / gsize;
+  const int first_m = g * a.group;
+  const int gm = min(a.group, a.tiles_m - first_m);
+  const int within = t - g * gsize;
+  tm = first_m + within % gm;
+  tn = within / gm;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float x, float y) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Scale 32 consecutive accumulator columns of one row and store them as bf16.
+template <bool kFloatAcc>
+__device__ __forceinline__ void store_c32(const MainArgs& a, const uint32_t* v, int64_t row,
+                                          int col0, float row_scale) {
+  if (row >= a.M) return;
+  const float4* sb = reinterpret_cast<const float4*>(a.sB + col0);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = col0 + 8 * j;
+    if (c + 8 > a.N) break;
+    float4 b0 = sb[2 * j], b1 = sb[2 * j + 1];
+    float f[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      f[i] = kFloatAcc ? __uint_as_float(v[8 * j + i]) : float(int(v[8 * j + i]));
+    uint4 o;
+    o.x = pack_bf16(f[0] * row_scale * b0.x, f[1] * row_scale * b0.y);
+    o.y = pack_bf16(f[2] * row_scale * b0.z, f[3] * row_scale * b0.w);
+    o.z = pack_bf16(f[4] * row_scale * b1.x, f[5] * row_scale * b1.y);
+    o.w = pack_bf16(f[6] * row_scale * b1.z, f[7] * row_scale * b1.w);
+    *reinterpret_cast<uint4*>(a.C + row * int64_t(a.N) + c) = o;
+  }
+}
+
+// Rotate-xor `f` into word (chunk % 16) of a register-resident transcript.
+__device__ __forceinline__ void transcript_update(uint32_t* T, int chunk, uint32_t f) {
+  switch (chunk & 15) {
+#define PB2_TU(i) \
+  case i:         \
+    T[i] = rotl13(T[i]) ^ f; \
+    break;
+    PB2_TU(0) PB2_TU(1) PB2_TU(2) PB2_TU(3) PB2_TU(4) PB2_TU(5) PB2_TU(6) PB2_TU(7)
+    PB2_TU(8) PB2_TU(9) PB2_TU(10) PB2_TU(11) PB2_TU(12) PB2_TU(13) PB2_TU(14) PB2_TU(15)
+#undef PB2_TU
+  }
+}
+
+__device__ void publish_hit(const MainArgs& a, int tm, int tn, int row_in_tile, int cls,
+                            const uint32_t* digest) {
+  const uint32_t row_off = uint32_t(tm * BM + row_in_tile);
+  const uint32_t col_off = uint32_t(tn * BN + 2 * cls);
+  const unsigned slot = atomicAdd(&a.sync->hit_count, 1u);
+  if (a.hits && (long long)slot < a.hit_cap) {
+    uint32_t* h = a.hits + size_t(slot) * PB2_HIT_WORDS;
+    h[0] = row_off;
+    h[1] = col_off;
+    h[2] = uint32_t(tm);
+    h[3] = uint32_t(tn);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) h[4 + i] = digest[i];
+  }
+  if (a.header && atomicCAS(&a.sync->global_lock, 0, 1) == 0) {
+    SignalHeader* H = a.header;
+    H->gridDim[0] = gridDim.x; H->gridDim[1] = gridDim.y; H->gridDim[2] = gridDim.z;
+    H->blockDim[0] = blockDim.x; H->blockDim[1] = blockDim.y; H->blockDim[2] = blockDim.z;
+    H->blockIdx[0] = blockIdx.x; H->blockIdx[1] = blockIdx.y; H->blockIdx[2] = blockIdx.z;
+    H->tileCoord[0] = uint32_t(tm); H->tileCoord[1] = uint32_t(tn); H->tileCoord[2] = 0;
+    H->threadIdx[0] = threadIdx.x; H->threadIdx[1] = 0; H->threadIdx[2] = 0;
+    H->num_registers_per_thread = 128;
+    // Element j of the hash tile, in the reference's per-thread fragment
+    // order: (row r, col c), (r, c+1), (r+8, c), (r+8, c+1), then c += 8.
+    for (int j = 0; j < 128; ++j) {
+      H->thread_rows[j] = uint8_t(row_in_tile + 8 * ((j >> 1) & 1));
+      H->thread_cols[j] = uint8_t(2 * cls + (j & 1) + 8 * (j >> 2));
+    }
+    H->mma_size[0] = a.M; H->mma_size[1] = a.N; H->mma_size[2] = a.K;
+    H->mma_tile_size[0] = BM; H->mma_tile_size[1] = BN; H->mma_tile_size[2] = BK;
+    for (int i = 0; i < 8; ++i) H->target[i] = a.target[i];
+    __threadfence_system();
+    H->status = 1;
+    __threadfence_system();
+    atomicExch(&a.sync->status, 1);
+  }
+}
+
+template <bool kReduce, bool kDenoise, bool kDebug>
+__global__ void __launch_bounds__(kThreads, 2) noisy_gemm_kernel(const __grid_constant__ MainArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stage_mem = base;
+  Smem& S = *reinterpret_cast<Smem*>(base + kStages * kStageBytes);
+  volatile int* abort_flag = &S.abort_flag;
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int nkb = a.K / BK;
+  const int nden = kDenoise ? 2 * (a.R / 64) : 0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&S.full[i], 1);
+      mbar_init(&S.empty[i], 1);
+    }
+    mbar_init(&S.acc_full, 1);
+    mbar_init(&S.acc_empty, 4);
+    mbar_init(&S.drain, 1);
+    S.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch(&a.tmA);
+    tma_prefetch(&a.tmB);
+    if (kDenoise) {
+      tma_prefetch(&a.tmDA0); tma_prefetch(&a.tmDB0);
+      tma_prefetch(&a.tmDA1); tma_prefetch(&a.tmDB1);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(&S.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = S.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int t = blockIdx.x; t < a.num_tiles && !*abort_flag; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(a, t, tm, tn);
+        const int m0 = tm * BM, n0 = tn * BN;
+        for (int kb = 0; kb < nkb + nden; ++kb, ++it) {
+          const int s = it % kStages;
+          if (!mbar_wait(&S.empty[s], ((it / kStages) & 1) ^ 1, abort_flag, a.sync)) break;
+          mbar_arrive_expect_tx(&S.full[s], kStageBytes);
+          uint8_t* sa = stage_mem + s * kStageBytes;
+          uint8_t* sb = sa + kAStage;
+          if (kb < nkb) {
+            tma_load_2d(&a.tmA, &S.full[s], sa, kb * BK, m0);
+            tma_load_2d(&a.tmB, &S.full[s], sb, kb * BK, n0);
+          } else {
+            const int d = kb - nkb;
+            const int per = a.R / 64;
+            const int col = (d % per) * 64;
+            const bool second = d >= per;
+            tma_load_2d(second ? &a.tmDA1 : &a.tmDA0, &S.full[s], sa, col, m0);
+            tma_load_2d(second ? &a.tmDB1 : &a.tmDB0, &S.full[s], sb, col, n0);
+          }
+        }
+      }
+      // Drain: wait (bounded) until every issued stage has landed before exit.
+      for (uint32_t j = (it > kStages ? it - kStages : 0); j < it; ++j) {
+        long long t0 = clock64();
+        while (!mbar_test(&S.full[j % kStages], (j / kStages) & 1) && clock64() - t0 < 100000000LL) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t it = 0;
+      uint32_t acc_parity = 0;
+      bool pending = false;  // an acc_full commit still awaits the epilogue's release
+      bool ok = true;
+      const uint32_t sbase = smem_u32(stage_mem);
+      for (int t = blockIdx.x; t < a.num_tiles && ok; t += gridDim.x) {
+        for (int kb = 0; kb < nkb + nden && ok; ++kb, ++it) {
+          const int s = it % kStages;
+          if (!(ok = mbar_wait(&S.full[s], (it / kStages) & 1, abort_flag, a.sync))) break;
+          tc_fence_after();
+          const uint64_t ad = sdesc_sw128(sbase + s * kStageBytes);
+          const uint64_t bd = sdesc_sw128(sbase + s * kStageBytes + kAStage);
+#pragma unroll
+          for (int ks = 0; ks < BK / 32; ++ks) {
+            if (pending) {
+              if (!(ok = mbar_wait(&S.acc_empty, acc_parity, abort_flag, a.sync))) break;
+              acc_parity ^= 1;
+              pending = false;
+              tc_fence_after();
+            }
+            if (kb < nkb) {
+              umma_i8(tmem, ad + 2 * ks, bd + 2 * ks, kIdescI8, (kb | ks) != 0);
+              if (kReduce && ((kb * BK + (ks + 1) * 32) % a.R) == 0) {
+                umma_commit(&S.acc_full);
+                pending = true;
+              }
+            } else {
+              umma_f16(tmem, ad + 2 * ks, bd + 2 * ks, kIdescF16, 1);
+            }
+          }
+          if (!ok) break;
+          umma_commit(&S.empty[s]);
+          // End of the main loop without transcript: hand the accumulator over.
+          if (!kReduce && kb == nkb - 1) {
+            umma_commit(&S.acc_full);
+            pending = true;
+          }
+          if (kDenoise && kb == nkb + nden - 1) {
+            umma_commit(&S.acc_full);
+            pending = true;
+          }
+        }
+      }
+      // Make sure every MMA has retired before TMEM is released.
+      umma_commit(&S.drain);
+      long long t0 = clock64();
+      while (!mbar_test(&S.drain, 0) && clock64() - t0 < 100000000LL) {
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = 32 * q + lane;
+    const uint32_t trow = tmem + (uint32_t(32 * q) << 16);
+    const bool is_low = (lane & 8) == 0;
+    const int cls0 = is_low ? 0 : 2;
+    const int tile_row = 32 * q + (lane & ~8);  // first row of this thread's hash tiles
+    const int nchunks = kReduce ? a.K / a.R : 0;
+    uint32_t acc_parity = 0;
+    bool ok = true;
+
+    for (int t = blockIdx.x; t < a.num_tiles && ok; t += gridDim.x) {
+      int tm, tn;
+      tile_coords(a, t, tm, tn);
+      const int64_t row = int64_t(tm) * BM + row_in_tile;
+      const int n0 = tn * BN;
+      const float sa = row < a.M ? a.sA[row] : 0.0f;
+      uint32_t T0[16], T1[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) T0[i] = T1[i] = 0;
+
+      // Sync points of this tile: one per transcript chunk (or one at the end
+      // without transcript), plus one after the denoise MMAs.
+      const int nsync = (kReduce ? nchunks : 1) + (kDenoise ? 1 : 0);
+      for (int sp = 0; sp < nsync; ++sp) {
+        if (!(ok = mbar_wait(&S.acc_full, acc_parity, abort_flag, a.sync))) break;
+        acc_parity ^= 1;
+        tc_fence_after();
+        const bool denoised = kDenoise && sp == nsync - 1;   // D is f32, final
+        const bool fold = kReduce && !denoised;
+        const bool last_int = !denoised && sp == (kReduce ? nchunks : 1) - 1;
+        uint32_t p0 = 0, p1 = 0, p2 = 0, p3 = 0;
+#pragma unroll 1
+        for (int b = 0; b < BN / 32; b += 2) {
+          uint32_t v[64];
+          __syncwarp();  // tcgen05.ld/st are .sync.aligned: reconverge after per-lane stores
+          tmem_ld32(trow + 32 * b, v);
+          tmem_ld32(trow + 32 * b + 32, v + 32);
+          tmem_wait_ld();
+          if (fold) {
+#pragma unroll
+            for (int i = 0; i < 64; i += 8) {
+              p0 ^= v[i] ^ v[i + 1];
+              p1 ^= v[i + 2] ^ v[i + 3];
+              p2 ^= v[i + 4] ^ v[i + 5];
+              p3 ^= v[i + 6] ^ v[i + 7];
+            }
+          }
+          if (denoised) {
+            store_c32<true>(a, v, row, n0 + 32 * b, sa * 4096.0f);
+            store_c32<true>(a, v + 32, row, n0 + 32 * b + 32, sa * 4096.0f);
+          } else if (last_int) {
+            if (kDenoise) {
+              // rewrite S as f32 * 2^-12 for the f16 denoise MMAs
+#pragma unroll
+              for (int i = 0; i < 64; ++i) v[i] = __float_as_uint(float(int(v[i])) * (1.0f / 4096.0f));
+              tmem_st32(trow + 32 * b, v);
+              tmem_st32(trow + 32 * b + 32, v + 32);
+            } else {
+              store_c32<false>(a, v, row, n0 + 32 * b, sa);
+              store_c32<false>(a, v + 32, row, n0 + 32 * b + 32, sa);
+            }
+          }
+        }
+        if (fold) {
+          const uint32_t s0 = is_low ? p2 : p0, s1 = is_low ? p3 : p1;
+          const uint32_t r0 = __shfl_xor_sync(0xffffffffu, s0, 8);
+          const uint32_t r1 = __shfl_xor_sync(0xffffffffu, s1, 8);
+          const uint32_t f0 = (is_low ? p0 : p2) ^ r0;
+          const uint32_t f1 = (is_low ? p1 : p3) ^ r1;
+          transcript_update(T0, sp, f0);
+          transcript_update(T1, sp, f1);
+          if (kDebug && lane == 0) atomicAdd(a.counter, 64ull);
+        }
+        __syncwarp();
+        if (kDenoise && last_int) tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.acc_empty);
+      }
+      if (!ok) break;
+
+      if (kReduce) {
+        uint32_t key[8], tgt[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          key[i] = a.key[i];
+          tgt[i] = a.target[i];
+        }
+        const int64_t grow = int64_t(tm) * BM + tile_row;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t* T = h == 0 ? T0 : T1;
+          const int cls = cls0 + h;
+          uint32_t dg[8];
+          b3_compress8(key, T, kB3SingleBlockKeyed, dg);
+          const int64_t gcol = int64_t(n0) + 2 * cls;
+          const bool in_bounds = (grow + 8 < a.M) && (gcol + 249 < a.N);
+          if (in_bounds && (a.transcripts || a.digests)) {
+            const int64_t idx = (grow / 16 * 8 + grow % 16) * (a.N / 64) + gcol / 256 * 4 + (gcol % 256) / 2;
+            if (a.transcripts)
+              for (int i = 0; i < 16; ++i) a.transcripts[idx * 16 + i] = T[i];
+            if (a.digests)
+              for (int i = 0; i < 8; ++i) a.digests[idx * 8 + i] = dg[i];
+          }
+          if (in_bounds && u256_le(dg, tgt)) publish_hit(a, tm, tn, tile_row, cls, dg);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host
+template <bool R_, bool D_, bool G_>
+int launch_variant(const MainArgs& a, int grid, cudaStream_t s) {
+  auto kern = noisy_gemm_kernel<R_, D_, G_>;
+  const int smem = kStages * kStageBytes + int(sizeof(Smem)) + 1024;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return launch_status();
+  kern<<<grid, kThreads, smem, s>>>(a);
+  return launch_status();
+}
+
+bool al16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+}  // namespace
+
+int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStream_t s) {
+  if (p.m <= 0 || p.n <= 0 || p.k <= 0) return PB2_ERR_INVALID_ARGUMENT;
+  if (p.tile_size_m != BM || p.tile_size_n != BN || p.tile_size_k != BK) return PB2_ERR_UNSUPPORTED_CONFIG;
+  if (p.cluster_size_m != 1 || p.cluster_size_n != 1) return PB2_ERR_UNSUPPORTED_CONFIG;
+  // pipeline_stages is a hint: the ring depth is fixed by the 2-CTA/SM layout.
+  if (p.k % BK != 0 || p.n % 8 != 0) return PB2_ERR_INVALID_ARGUMENT;
+  if (p.m > INT32_MAX || p.n > INT32_MAX || p.k > INT32_MAX) return PB2_ERR_INVALID_ARGUMENT;
+  if ((reduce || denoise) && !(p.r == 64 || p.r == 128 || p.r == 256)) return PB2_ERR_UNSUPPORTED_CONFIG;
+  if (reduce && (p.k % p.r != 0)) return PB2_ERR_INVALID_ARGUMENT;
+  if (!p.ApEA || !p.BpEB || !p.A_scales || !p.B_scales || !p.C) return PB2_ERR_INVALID_ARGUMENT;
+  if (!al16(p.ApEA) || !al16(p.BpEB) || !al16(p.C) || !al16(p.B_scales)) return PB2_ERR_INVALID_ARGUMENT;
+  if (reduce && (!p.host_signal_sync || !p.pow_target || !p.pow_key)) return PB2_ERR_INVALID_ARGUMENT;
+  if (denoise && (!p.EAL_fp16 || !p.EBR_fp16 || !p.AxEBL_fp16 || !p.EARxBpEB_fp16))
+    return PB2_ERR_INVALID_ARGUMENT;
+  const bool debug = reduce && p.enable_debug;
+  if (debug && !p.inner_hash_counter) return PB2_ERR_INVALID_ARGUMENT;
+  if ((p.transcripts || p.digests) && (p.m % 16 != 0 || p.n % 256 != 0)) return PB2_ERR_INVALID_ARGUMENT;
+
+  MainArgs a;
+  std::memset(&a, 0, sizeof(a));
+  int st;
+  if ((st = make_tmap_2d(&a.tmA, p.ApEA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.k, p.m, BK, BM,
+                         CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  if ((st = make_tmap_2d(&a.tmB, p.BpEB, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.k, p.n, BK, BN,
+                         CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  if (denoise) {
+    const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    if ((st = make_tmap_2d(&a.tmDA0, p.EAL_fp16, F16, 2, p.r, p.m, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+        (st = make_tmap_2d(&a.tmDB0, p.EARxBpEB_fp16, F16, 2, p.r, p.n, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+        (st = make_tmap_2d(&a.tmDA1, p.AxEBL_fp16, F16, 2, p.r, p.m, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+        (st = make_tmap_2d(&a.tmDB1, p.EBR_fp16, F16, 2, p.r, p.n, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
+  }
+  a.M = int(p.m);
+  a.N = int(p.n);
+  a.K = int(p.k);
+  a.R = int(p.r);
+  a.tiles_m = int((p.m + BM - 1) / BM);
+  a.tiles_n = int((p.n + BN - 1) / BN);
+  a.num_tiles = a.tiles_m * a.tiles_n;
+  a.group = p.swizzle > 0 ? p.swizzle : 16;
+  if (a.group > a.tiles_m) a.group = a.tiles_m;
+  a.sA = p.A_scales;
+  a.sB = p.B_scales;
+  a.C = static_cast<__nv_bfloat16*>(p.C);
+  a.sync = static_cast<SignalSync*>(p.host_signal_sync);
+  a.header = static_cast<SignalHeader*>(p.host_signal_header_pinned);
+  a.target = p.pow_target;
+  a.key = p.pow_key;
+  a.counter = reinterpret_cast<unsigned long long*>(p.inner_hash_counter);
+  a.hits = p.hits;
+  a.hit_cap = p.hits ? p.hit_capacity : 0;
+  a.transcripts = p.transcripts;
+  a.digests = p.digests;
+
+  const int sms = sm_count(p.device);
+  const int grid = std::min(a.num_tiles, 2 * (sms > 0 ? sms : 148));
+  if (reduce && denoise) return debug ? launch_variant<true, true, true>(a, grid, s)
+                                      : launch_variant<true, true, false>(a, grid, s);
+  if (reduce) return debug ? launch_variant<true, false, true>(a, grid, s)
+                           : launch_variant<true, false, false>(a, grid, s);
+  if (denoise) return launch_variant<false, true, false>(a, grid, s);
+  return launch_variant<false, false, false>(a, grid, s);
+}
+
+int denoise_convert(const int32_t* in, void* out, int64_t count, float scale, cudaStream_t s);
+
+}  // namespace pb2
+
+extern "C" int pb2_noisy_gemm(const pb2_gemm_params* pp, void* stream) {
+  using namespace pb2;
+  if (!pp) return PB2_ERR_INVALID_ARGUMENT;
+  const pb2_gemm_params& p = *pp;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int st = set_device(p.device);
+  if (st) return st;
+  if (p.run_noising_a) {
+    if (!p.A || !p.EAL || !p.EAR_R_major || !p.EBL_K_major) return PB2_ERR_INVALID_ARGUMENT;
+    pb2_noising_params q{};
+    q.device = p.device; q.rows = p.m; q.k = p.k; q.r = p.r;
+    q.X = p.A; q.EL = p.EAL; q.E_rmajor = p.EAR_R_major; q.E_kmajor = p.EBL_K_major;
+    q.XpE = p.ApEA;
+    q.proj = p.AxEBL_int32 ? static_cast<void*>(p.AxEBL_int32) : p.AxEBL_fp16;
+    q.proj_is_fp16 = p.AxEBL_int32 ? 0 : 1;
+    q.k_blocks_per_split = p.AxEBL_int32 ? p.k_blocks_per_split_noising_a : 0;
+    if ((st = pb2_noise_A(&q, stream))) return st;
+  }
+  if (p.run_noising_b) {
+    if (!p.B || !p.EBR || !p.EAR_K_major || !p.EBL_R_major) return PB2_ERR_INVALID_ARGUMENT;
+    pb2_noising_params q{};
+    q.device = p.device; q.rows = p.n; q.k = p.k; q.r = p.r;
+    q.X = p.B; q.EL = p.EBR; q.E_rmajor = p.EBL_R_major; q.E_kmajor = p.EAR_K_major;
+    q.XpE = p.BpEB;
+    q.proj = p.EARxBpEB_int32 ? static_cast<void*>(p.EARxBpEB_int32) : p.EARxBpEB_fp16;
+    q.proj_is_fp16 = p.EARxBpEB_int32 ? 0 : 1;
+    q.k_blocks_per_split = p.EARxBpEB_int32 ? p.k_blocks_per_split_noising_b : 0;
+    if ((st = pb2_noise_B(&q, stream))) return st;
+  }
+  if (!p.skip_denoising) {
+    if (p.AxEBL_int32 && (st = denoise_convert(p.AxEBL_int32, p.AxEBL_fp16, p.m * p.r, 1.0f / 16384.0f, s)))
+      return st;
+    if (p.EARxBpEB_int32 &&
+        (st = denoise_convert(p.EARxBpEB_int32, p.EARxBpEB_fp16, p.n * p.r, 1.0f / 4096.0f, s)))
+      return st;
+  }
+  return run_main_kernel(p, !p.skip_reduction, !p.skip_denoising, s);
+}
+
+extern "C" int pb2_gemm(const pb2_gemm_params* pp, void* stream) {
+  using namespace pb2;
+  if (!pp) return PB2_ERR_INVALID_ARGUMENT;
+  int st = set_device(pp->device);
+  if (st) return st;
+  return run_main_kernel(*pp, false, false, static_cast<cudaStream_t>(stream));
+}

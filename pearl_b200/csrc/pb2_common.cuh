@@ -1,0 +1,328 @@
+// pb2_common.cuh -- sm_100a building blocks shared by the pearl_b200 kernels:
+// status codes, bounded mbarrier waits, TMA loads, tcgen05 (UMMA / TMEM)
+// wrappers and a register-resident BLAKE3 compression.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/pearl_b200.h"
+
+namespace pb2 {
+
+// ---------------------------------------------------------------------------
+// Device-side status word layout (the caller's host_signal_sync buffer).
+// The first two ints match the reference's HostSignalSync
+// (miner/pearl-gemm/csrc/gemm/host_signal_header.hpp:9-12); the B200 build
+// appends a hit counter and an error code.
+// ---------------------------------------------------------------------------
+struct __align__(8) SignalSync {
+  int global_lock;
+  int status;
+  unsigned int hit_count;
+  int error;
+};
+static_assert(sizeof(SignalSync) == PB2_HOST_SIGNAL_SYNC_SIZE, "sync size");
+
+// Reference-compatible HostSignalHeader (host_signal_header.hpp:21-50):
+// identical field order, sizes and 128-byte alignment so callers that read the
+// pinned header (pearl_gemm.helpers.extract_indices) see the same bytes.
+struct __align__(128) SignalHeader {
+  int status;
+  uint32_t gridDim[3];
+  uint32_t blockDim[3];
+  uint32_t blockIdx[3];
+  uint32_t tileCoord[3];
+  uint32_t threadIdx[3];
+  uint16_t num_registers_per_thread;
+  uint8_t thread_rows[256];
+  uint8_t thread_cols[256];
+  int mma_size[3];
+  int mma_tile_size[3];
+  uint32_t target[8];
+};
+static_assert(sizeof(SignalHeader) == PB2_HOST_SIGNAL_HEADER_SIZE, "header size");
+
+// Spin budget of every device-side wait, in SM clock cycles (~1 s at the
+// B200's clocks).  Nothing legitimate waits longer than microseconds; a wait
+// that runs out records PB2_ERR_DEVICE_TIMEOUT and the kernel unwinds.
+constexpr long long kWaitBudgetCycles = 2000000000LL;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void record_error(SignalSync* sync, int code) {
+  if (sync) atomicCAS(&sync->error, 0, code);
+}
+
+// ------------------------------------------------------------------ mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase with the given parity.  Returns false (and
+// records the error / raises the CTA abort flag) if the budget runs out or
+// another warp of the CTA already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          SignalSync* sync) {
+  if (mbar_test(bar, parity)) return true;
+  long long t0 = clock64();
+  while (true) {
+    if (mbar_test(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitBudgetCycles) {
+      *abort_flag = 1;
+      record_error(sync, PB2_ERR_DEVICE_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ TMA
+__device__ __forceinline__ void tma_prefetch(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+// 2-D tiled load into this CTA's shared memory (no multicast).
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// ------------------------------------------------------------------ tcgen05
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+// Arrive on `bar` once every tcgen05.mma issued so far by this thread is done.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+// D(tmem) (+)= A(smem desc) * B(smem desc)^T, int8 x int8 -> int32.
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D(tmem) (+)= A * B^T, f16 x f16 -> f32.
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Instruction descriptor (PTX ISA "instruction descriptor" table for
+// kind::f16 / kind::i8): dense, K-major A and B.
+//   [4,6) D format (1 = f32, 2 = s32)  [7,10) A format  [10,13) B format
+//   [17,23) N >> 3                     [24,29) M >> 4
+__host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+}
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+}
+
+// Shared-memory matrix descriptor for a K-major operand tile stored with the
+// 128-byte swizzle (rows of 128 bytes, 8-row / 1024-byte swizzle atoms), the
+// layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B.
+//   [0,14) start >> 4   [16,30) LBO >> 4 (unused for swizzled K-major: 1)
+//   [32,46) SBO >> 4 (1024 B between 8-row groups)   [46,48) version = 1
+//   [61,64) layout: 2 = SWIZZLE_128B
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= uint64_t((smem_addr >> 4) & 0x3FFF);
+  d |= uint64_t(1) << 16;
+  d |= uint64_t(1024 >> 4) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(2) << 61;
+  return d;
+}
+
+// TMEM loads/stores, 32 lanes x 32 bit shape: thread i of the warp accesses
+// lane (base_lane + i); register j holds column (base_col + j).
+#define PB2_R8(p, o) "=r"(p[o + 0]), "=r"(p[o + 1]), "=r"(p[o + 2]), "=r"(p[o + 3]), \
+    "=r"(p[o + 4]), "=r"(p[o + 5]), "=r"(p[o + 6]), "=r"(p[o + 7])
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* v) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : PB2_R8(v, 0), PB2_R8(v, 8), PB2_R8(v, 16), PB2_R8(v, 24)
+      : "r"(taddr)
+      : "memory");
+}
+#undef PB2_R8
+#define PB2_W8(p, o) "r"(p[o + 0]), "r"(p[o + 1]), "r"(p[o + 2]), "r"(p[o + 3]), \
+    "r"(p[o + 4]), "r"(p[o + 5]), "r"(p[o + 6]), "r"(p[o + 7])
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      PB2_W8(v, 0), PB2_W8(v, 8), PB2_W8(v, 16), PB2_W8(v, 24)
+      : "memory");
+}
+#undef PB2_W8
+
+// ------------------------------------------------------------------ BLAKE3
+// Register-resident BLAKE3 compression (published BLAKE3 specification).
+// The message schedule of each of the 7 rounds is computed at compile time so
+// every message-word index is static and the 16 words stay in registers.
+struct B3Schedule {
+  uint8_t s[7][16];
+};
+__host__ __device__ constexpr B3Schedule make_b3_schedule() {
+  constexpr uint8_t perm[16] = {2, 6, 3, 10, 7, 0, 4, 13, 1, 11, 12, 5, 9, 14, 15, 8};
+  B3Schedule r{};
+  for (int i = 0; i < 16; ++i) r.s[0][i] = uint8_t(i);
+  for (int k = 1; k < 7; ++k)
+    for (int i = 0; i < 16; ++i) r.s[k][i] = r.s[k - 1][perm[i]];
+  return r;
+}
+constexpr B3Schedule kB3Sched = make_b3_schedule();
+
+constexpr uint32_t kB3IV0 = 0x6A09E667u, kB3IV1 = 0xBB67AE85u, kB3IV2 = 0x3C6EF372u,
+                   kB3IV3 = 0xA54FF53Au;
+constexpr uint32_t kB3ChunkStart = 1, kB3ChunkEnd = 2, kB3Root = 8, kB3Keyed = 16;
+// Flags of a single-block keyed hash: the whole input is one 64-byte block.
+constexpr uint32_t kB3SingleBlockKeyed = kB3ChunkStart | kB3ChunkEnd | kB3Root | kB3Keyed;
+
+__device__ __forceinline__ uint32_t rotr32(uint32_t x, int n) { return __funnelshift_r(x, x, n); }
+
+#define PB2_B3_G(a, b, c, d, x, y)        \
+  do {                                    \
+    v[a] = v[a] + v[b] + (x);             \
+    v[d] = rotr32(v[d] ^ v[a], 16);       \
+    v[c] = v[c] + v[d];                   \
+    v[b] = rotr32(v[b] ^ v[c], 12);       \
+    v[a] = v[a] + v[b] + (y);             \
+    v[d] = rotr32(v[d] ^ v[a], 8);        \
+    v[c] = v[c] + v[d];                   \
+    v[b] = rotr32(v[b] ^ v[c], 7);        \
+  } while (0)
+
+template <int R>
+__device__ __forceinline__ void b3_round(uint32_t* v, const uint32_t* m) {
+  constexpr B3Schedule S = kB3Sched;
+  PB2_B3_G(0, 4, 8, 12, m[S.s[R][0]], m[S.s[R][1]]);
+  PB2_B3_G(1, 5, 9, 13, m[S.s[R][2]], m[S.s[R][3]]);
+  PB2_B3_G(2, 6, 10, 14, m[S.s[R][4]], m[S.s[R][5]]);
+  PB2_B3_G(3, 7, 11, 15, m[S.s[R][6]], m[S.s[R][7]]);
+  PB2_B3_G(0, 5, 10, 15, m[S.s[R][8]], m[S.s[R][9]]);
+  PB2_B3_G(1, 6, 11, 12, m[S.s[R][10]], m[S.s[R][11]]);
+  PB2_B3_G(2, 7, 8, 13, m[S.s[R][12]], m[S.s[R][13]]);
+  PB2_B3_G(3, 4, 9, 14, m[S.s[R][14]], m[S.s[R][15]]);
+}
+#undef PB2_B3_G
+
+// out[0..8) = first half of compress(cv, m, counter=0, block_len=64, flags).
+__device__ __forceinline__ void b3_compress8(const uint32_t* cv, const uint32_t* m,
+                                             uint32_t flags, uint32_t* out) {
+  uint32_t v[16];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = cv[i];
+  v[8] = kB3IV0;
+  v[9] = kB3IV1;
+  v[10] = kB3IV2;
+  v[11] = kB3IV3;
+  v[12] = 0;
+  v[13] = 0;
+  v[14] = 64;
+  v[15] = flags;
+  b3_round<0>(v, m);
+  b3_round<1>(v, m);
+  b3_round<2>(v, m);
+  b3_round<3>(v, m);
+  b3_round<4>(v, m);
+  b3_round<5>(v, m);
+  b3_round<6>(v, m);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) out[i] = v[i] ^ v[i + 8];
+}
+
+// uint256 (8 little-endian words, word 7 most significant): a <= b.
+__device__ __forceinline__ bool u256_le(const uint32_t* a, const uint32_t* b) {
+  bool decided = false, le = true;
+#pragma unroll
+  for (int i = 7; i >= 0; --i) {
+    if (!decided && a[i] != b[i]) {
+      decided = true;
+      le = a[i] < b[i];
+    }
+  }
+  return le;
+}
+
+__device__ __forceinline__ uint32_t rotl13(uint32_t x) { return __funnelshift_l(x, x, 13); }
+
+}  // namespace pb2
+
+// Host helpers (pb2_host.cu).
+namespace pb2 {
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
+                 uint64_t inner, uint64_t outer, uint32_t box_inner, uint32_t box_outer,
+                 CUtensorMapSwizzle swizzle);
+int set_device(int device);
+int sm_count(int device);
+int launch_status();
+}  // namespace pb2
