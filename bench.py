@@ -1,0 +1,434 @@
+"""Benchmark of the Pearl mining hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: one mined int8 noisy GEMM, M = N = K = 8192,
+R = 128, seeded int7 operands, int32 accumulation, fused transcript hashing,
+keyed BLAKE3 and a difficulty check whose target yields ~1e-6 hits per hash
+tile.  One step = noise_gen + noise_A + noise_B + the mined GEMM (transcript,
+BLAKE3, target compare, denoise, bf16 C) for one GEMM; each step uses a fresh
+pair of noise seeds (another point of the nonce space).  Under torchrun every
+rank mines its own seeds (nonce-space sharding, no collective on the data
+path; weak scaling) and only hit counts are reduced after timing.
+
+metric: effective TOPS = 2*M*N*K per GEMM / time (noise and denoise work not
+counted); hashed tiles/s = M*N/128 per GEMM / time.
+
+--impl reference times the reference's CPU path on the host cores: the C
+restatement in oracle/ (the Rust miner zk-pow/src/ffi/mine.rs cannot be built
+here: no cargo), each step a bounded sample of hash tiles of the same GEMM.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M = N = K = 8192
+R = 128
+HASH_TILE = 128  # elements per protocol hash tile (2 x 64)
+TARGET_FRACTION = 1e-6  # expected hits per hash tile
+# Kernels launched per step by this implementation (noise_gen 1, noise_A 2,
+# noise_B 2, mined GEMM 1).
+LAUNCHES_PER_STEP = 6
+
+
+def target_value(frac: float) -> int:
+    return int(frac * (1 << 256))
+
+
+def measured_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return json.load(open(p))
+    return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0,
+            "fallback": True}
+
+
+def ncu_traffic() -> dict | None:
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    return json.load(open(p)) if os.path.exists(p) else None
+
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"pb2_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait()
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9 and f[1].isdigit():
+                rows.append(f)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [int(r[1]) for r in rows]
+        loaded = [s for s in sm if s > 500] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": int(rows[0][2]),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def setup_dist(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        if args.impl == "ours":
+            torch.cuda.set_device(local)
+        dist.init_process_group("nccl" if args.impl == "ours" else "gloo",
+                                timeout=datetime.timedelta(seconds=120))
+    return world, rank, local
+
+
+# ------------------------------------------------------------------ ours ---
+def run_ours(args, world, rank, local):
+    import pearl_b200 as pg
+    from tests.gpu_problem import make_problem, signal_buffers
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    p = make_problem(M, N, K, R, seed=1000 + rank, device=dev)
+    # A fresh pair of noise seeds every step (distinct points of the nonce
+    # space), all resident on the device before timing.
+    n_keys = args.warmup + args.steps
+    g = torch.Generator().manual_seed(97 + rank)
+    keys_a = torch.randint(0, 256, (n_keys, 32), dtype=torch.uint8, generator=g).to(dev)
+    keys_b = torch.randint(0, 256, (n_keys, 32), dtype=torch.uint8, generator=g).to(dev)
+    target = pg.make_pow_target_tensor(target_value(TARGET_FRACTION), dev)
+    header, sync = signal_buffers(dev)
+    hits = torch.zeros(1024, 12, dtype=torch.uint32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ev_main = []
+
+    def step(i, record=False):
+        # host_signal_sync is zeroed once before the timed loop, so hit_count
+        # accumulates over the steps (the header keeps the first hit).
+        ka, kb = keys_a[i % n_keys], keys_b[i % n_keys]
+        pg.noise_gen(R=R, key_A=ka, key_B=kb, **p.noise)
+        pg.noise_A(p.A, p.noise["EAL"], p.out["AxEBL_fp16"], p.out["ApEA"],
+                   EAR=p.noise["EAR_R_major"], EBL=p.noise["EBL_K_major"])
+        pg.noise_B(p.B, p.noise["EBR"], p.out["EARxBpEB_fp16"], p.out["BpEB"],
+                   EAR=p.noise["EAR_K_major"], EBL=p.noise["EBL_R_major"])
+        if record:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        pg.noisy_gemm(A=p.A, B=p.B, A_scales=p.A_scales, B_scales=p.B_scales,
+                      host_signal_header_pinned=header, host_signal_sync=sync, pow_target=target,
+                      pow_key=ka.view(torch.uint32), run_noising_A=False, run_noising_B=False,
+                      hits=hits, **p.noise, **p.out)
+        if record:
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record(stream)
+            ev_main.append((e0, e1))
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    err = pg.get_host_signal_sync_fields(sync)["error"]
+    if err:
+        raise RuntimeError(f"device reported error {err}")
+    sync.zero_()
+    barrier(world)
+    clocks = ClockSampler(dev.index if dev.index is not None else 0)
+    clocks.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        step(args.warmup + i, record=True)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1)
+    main_ms = sum(a.elapsed_time(b) for a, b in ev_main) / len(ev_main)
+    total_hits = int(pg.get_host_signal_sync_fields(sync)["hit_count"])
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        h = torch.tensor([total_hits], device=dev)
+        dist.all_reduce(h)
+        total_hits = int(h.item())
+
+    # ---- end to end through the public API with host buffers -------------
+    e2e = run_e2e(args, p, keys_a, keys_b, target, header, sync, dev, world)
+
+    # ---- live cuBLAS int8 reference point (rank 0) ------------------------
+    cublas = None
+    if rank == 0:
+        try:
+            for _ in range(3):
+                torch._int_mm(p.A, p.B.t())
+            torch.cuda.synchronize(dev)
+            a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+            a.record(stream)
+            for _ in range(10):
+                torch._int_mm(p.A, p.B.t())
+            b.record(stream)
+            torch.cuda.synchronize(dev)
+            cublas = 2 * M * N * K / (a.elapsed_time(b) / 10 * 1e-3) / 1e12
+        except Exception:  # noqa: BLE001
+            cublas = None
+
+    if rank != 0:
+        return None
+    ops = 2.0 * M * N * K
+    tiles = M * N / HASH_TILE
+    step_s = ms / args.steps * 1e-3
+    peaks = measured_peaks()
+    peak_int8 = 2.0 * peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    achieved = ops / (main_ms * 1e-3) / 1e12
+    traffic = ncu_traffic()
+    line = {
+        "metric": "effective TOPS (mined int8 noisy GEMM with fused transcript hashing)",
+        "value": round(world * ops / step_s / 1e12, 2),
+        "unit": "TOPS",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int8",
+        "data": "synthetic (seeded int7 operands, fresh noise seeds per step)",
+        "config": {"workload": "pearl-gemm noisy_gemm M=N=K=8192 R=128, target 1e-6 hits/hash tile",
+                   "m": M, "n": N, "k": K, "r": R, "hash_tile": "2x64",
+                   "l2": "inputs larger than L2: A,B,ApEA,BpEB,C = 384 MiB per step > 126 MB",
+                   "parallelism": f"nonce-space shards x{world}"},
+        "hashed_tiles_per_s": round(world * tiles / step_s, 1),
+        "hits": total_hits,
+        "expected_hits": round(world * args.steps * tiles * TARGET_FRACTION, 2),
+        "main_kernel_ms": round(main_ms, 4),
+        "e2e": e2e,
+        "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+        "roofline": {
+            "kernel": "noisy_gemm_kernel<reduce,denoise> (tcgen05 kind::i8 + transcript + BLAKE3)",
+            "bound": "tensor",
+            "achieved": round(achieved, 1),
+            "peak": round(peak_int8, 1),
+            "unit": "TOPS",
+            "frac": round(achieved / peak_int8, 4),
+            "peak_source": "2 x measured sustained bf16 (MEASURED_PEAKS.json; B200 dense int8 = 2x bf16)",
+            "frac_of_burst": round(achieved / (2.0 * peaks["bf16_tflops"]), 4),
+            "cublas_int8_live_tops": round(cublas, 1) if cublas else None,
+            "traffic": traffic.get("main_kernel_dram_bytes_per_launch") if traffic else None,
+        },
+        "clocks": clk,
+    }
+    line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
+    return line
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def run_e2e(args, p, keys_a, keys_b, target, header, sync, dev, world):
+    """Same metric through the public call a miner makes (noise_gen +
+    noisy_gemm with noising), inputs copied from pinned host memory every step
+    and the step's result (sync word + hit list) read back."""
+    import pearl_b200 as pg
+
+    hostA = p.A.cpu().pin_memory()
+    hostB = p.B.cpu().pin_memory()
+    hit_host = torch.zeros(64, 12, dtype=torch.uint32).pin_memory()
+    sync_host = torch.zeros(16, dtype=torch.int8).pin_memory()
+    hits = torch.zeros(64, 12, dtype=torch.uint32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    steps = max(1, min(args.steps, args.e2e_steps))
+
+    def step(i):
+        p.A.copy_(hostA, non_blocking=True)
+        p.B.copy_(hostB, non_blocking=True)
+        sync.zero_()
+        ka, kb = keys_a[i % len(keys_a)], keys_b[i % len(keys_b)]
+        pg.noise_gen(R=R, key_A=ka, key_B=kb, **p.noise)
+        pg.noisy_gemm(A=p.A, B=p.B, A_scales=p.A_scales, B_scales=p.B_scales,
+                      host_signal_header_pinned=header, host_signal_sync=sync, pow_target=target,
+                      pow_key=ka.view(torch.uint32), hits=hits, **p.noise, **p.out)
+        sync_host.copy_(sync, non_blocking=True)
+        hit_host.copy_(hits, non_blocking=True)
+
+    for i in range(3):
+        step(i)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+    a.record(stream)
+    for i in range(steps):
+        step(i)
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b)
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    step_s = ms / steps * 1e-3
+    return {"value": round(world * 2.0 * M * N * K / step_s / 1e12, 2), "unit": "TOPS",
+            "h2d_bytes_per_step": 2 * M * K, "d2h_bytes_per_step": 16 + hit_host.numel() * 4,
+            "steps": steps, "ms_per_step": round(ms / steps, 4),
+            "path": "pearl_b200.noise_gen + pearl_b200.noisy_gemm (run_noising_A/B) from pinned host A,B"}
+
+
+# ------------------------------------------------------- CPU reference ----
+class CpuProblem:
+    """The config-2 GEMM prepared for the oracle: operands, noise, noised
+    operands (the per-GEMM O(MK) part is timed once and amortized)."""
+
+    def __init__(self, seed=1000):
+        import numpy as np
+
+        from oracle import oracle as O
+        from tests.gpu_problem import random_key, seeded_operands
+        self.O = O
+        A, B = seeded_operands(M, N, K, seed)
+        self.key_a, self.key_b = random_key(seed + 1000), random_key(seed + 2000)
+        t = time.perf_counter()
+        prob = O.noisy_problem(A.numpy(), B.numpy(), self.key_a, self.key_b, R)
+        self.noise_s = time.perf_counter() - t
+        self.ApEA, self.BpEB = prob.ApEA, prob.BpEB
+        self.total_tiles = O.num_hash_tiles(M, N)
+        self.rng = np.random.default_rng(seed)
+        self.target = target_value(TARGET_FRACTION)
+
+    def tiles_time(self, count: int) -> float:
+        start = int(self.rng.integers(0, self.total_tiles - count))
+        t = time.perf_counter()
+        self.O.mine_tiles(self.ApEA, self.BpEB, R, self.key_a, self.target, start, start + count)
+        return time.perf_counter() - t
+
+    def gemm_seconds(self, tiles: int, secs: float) -> float:
+        return self.noise_s + secs / tiles * self.total_tiles
+
+
+def cpu_baseline(budget_s: float = 12.0) -> dict:
+    from oracle import oracle as O
+    cp = CpuProblem()
+    per = cp.tiles_time(64) / 64
+    count = max(64, int(budget_s / max(per, 1e-6)))
+    secs = cp.tiles_time(count)
+    gemm_s = cp.gemm_seconds(count, secs)
+    return {"value": round(2.0 * M * N * K / gemm_s / 1e12, 6), "unit": "TOPS",
+            "cores": O.num_threads(), "kind": "port",
+            "hashed_tiles_per_s": round(cp.total_tiles / gemm_s, 1),
+            "sample": (f"{count} of {cp.total_tiles} hash tiles of the 8192^3 GEMM (full K, "
+                       f"{secs:.1f}s) + full noise/noising ({cp.noise_s:.2f}s), extrapolated per tile"),
+            "cpu": cpu_model()}
+
+
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return None
+    from oracle import oracle as O
+    cp = CpuProblem()
+    per = cp.tiles_time(16) / 16
+    # size the per-step sample so the whole run stays within ~args.ref_budget seconds
+    per_step = max(1, int(args.ref_budget / max(1, args.steps + args.warmup) / max(per, 1e-6)))
+    for _ in range(args.warmup):
+        cp.tiles_time(per_step)
+    secs = sum(cp.tiles_time(per_step) for _ in range(args.steps))
+    tiles = per_step * args.steps
+    gemm_s = cp.gemm_seconds(tiles, secs)
+    value = round(2.0 * M * N * K / gemm_s / 1e12, 6)
+    sample = (f"{per_step} hash tiles (full K) per step of the 8192^3 GEMM, amortized noise/noising "
+              f"({cp.noise_s:.2f}s per GEMM); GEMM time extrapolated per tile")
+    return {
+        "impl": "reference",
+        "metric": "effective TOPS (mined int8 noisy GEMM with fused transcript hashing)",
+        "value": value, "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded int7 operands)",
+        "config": {"workload": "pearl-gemm noisy_gemm M=N=K=8192 R=128, target 1e-6 hits/hash tile",
+                   "m": M, "n": N, "k": K, "r": R,
+                   "implementation": "oracle/pearl_oracle.c: C restatement of zk-pow/src/ffi/mine.rs "
+                                     "(Rust toolchain absent, reference miner not buildable)"},
+        "hashed_tiles_per_s": round(cp.total_tiles / gemm_s, 1),
+        "cpu_baseline": {"value": value, "unit": "TOPS", "cores": O.num_threads(), "kind": "port",
+                         "sample": sample, "cpu": cpu_model()},
+        "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=40)
+    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--ref-budget", type=float, default=90.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = setup_dist(args)
+    try:
+        if args.impl == "reference":
+            line = run_reference(args, world, rank)
+        else:
+            line = run_ours(args, world, rank, local)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

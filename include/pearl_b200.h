@@ -111,6 +111,7 @@ typedef struct pb2_noising_params {
   void* proj;             /* (rows,r) out, int32 or half */
   int proj_is_fp16;
   int k_blocks_per_split; /* <0: heuristic; 0: no split; >0: k-blocks of 128 per CTA */
+  void* host_signal_sync; /* optional: receives PB2_ERR_DEVICE_TIMEOUT in its error word */
 } pb2_noising_params;
 PB2_API int pb2_noise_A(const pb2_noising_params* p, void* stream);
 PB2_API int pb2_noise_B(const pb2_noising_params* p, void* stream);

@@ -45,7 +45,8 @@ class NoiseGenParams(ctypes.Structure):
 class NoisingParams(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int), ("rows", _i64), ("k", _i64), ("r", _i64),
                 ("X", _vp), ("EL", _vp), ("E_rmajor", _vp), ("E_kmajor", _vp), ("XpE", _vp),
-                ("proj", _vp), ("proj_is_fp16", ctypes.c_int), ("k_blocks_per_split", ctypes.c_int)]
+                ("proj", _vp), ("proj_is_fp16", ctypes.c_int), ("k_blocks_per_split", ctypes.c_int),
+                ("host_signal_sync", _vp)]
 
 
 class DenoiseConverterParams(ctypes.Structure):

@@ -435,7 +435,7 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
   if (p.k % BK != 0 || p.n % 8 != 0) return PB2_ERR_INVALID_ARGUMENT;
   if (p.m > INT32_MAX || p.n > INT32_MAX || p.k > INT32_MAX) return PB2_ERR_INVALID_ARGUMENT;
   if ((reduce || denoise) && !(p.r == 64 || p.r == 128 || p.r == 256)) return PB2_ERR_UNSUPPORTED_CONFIG;
-  if (reduce && (p.k % p.r != 0)) return PB2_ERR_INVALID_ARGUMENT;
+  if ((reduce || denoise) && (p.k % p.r != 0)) return PB2_ERR_INVALID_ARGUMENT;
   if (!p.ApEA || !p.BpEB || !p.A_scales || !p.B_scales || !p.C) return PB2_ERR_INVALID_ARGUMENT;
   if (!al16(p.ApEA) || !al16(p.BpEB) || !al16(p.C) || !al16(p.B_scales)) return PB2_ERR_INVALID_ARGUMENT;
   if (reduce && (!p.host_signal_sync || !p.pow_target || !p.pow_key)) return PB2_ERR_INVALID_ARGUMENT;
@@ -514,6 +514,7 @@ extern "C" int pb2_noisy_gemm(const pb2_gemm_params* pp, void* stream) {
     q.proj = p.AxEBL_int32 ? static_cast<void*>(p.AxEBL_int32) : p.AxEBL_fp16;
     q.proj_is_fp16 = p.AxEBL_int32 ? 0 : 1;
     q.k_blocks_per_split = p.AxEBL_int32 ? p.k_blocks_per_split_noising_a : 0;
+    q.host_signal_sync = p.host_signal_sync;
     if ((st = pb2_noise_A(&q, stream))) return st;
   }
   if (p.run_noising_b) {
@@ -525,6 +526,7 @@ extern "C" int pb2_noisy_gemm(const pb2_gemm_params* pp, void* stream) {
     q.proj = p.EARxBpEB_int32 ? static_cast<void*>(p.EARxBpEB_int32) : p.EARxBpEB_fp16;
     q.proj_is_fp16 = p.EARxBpEB_int32 ? 0 : 1;
     q.k_blocks_per_split = p.EARxBpEB_int32 ? p.k_blocks_per_split_noising_b : 0;
+    q.host_signal_sync = p.host_signal_sync;
     if ((st = pb2_noise_B(&q, stream))) return st;
   }
   if (!p.skip_denoising) {

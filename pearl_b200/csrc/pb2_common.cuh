@@ -117,6 +117,57 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
+// Named barrier among `count` threads (a multiple of 32) of the CTA.
+__device__ __forceinline__ void named_barrier_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// ------------------------------------------------------------------ cluster
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// All threads of every CTA of the cluster: arrive (release) and wait (acquire).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Shared::cluster address of `local` in the CTA of rank `rank`.
+__device__ __forceinline__ uint32_t mapa(const void* local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar)
+               : "memory");
+}
+__device__ __forceinline__ int4 ld_cluster_v4(uint32_t addr) {
+  int4 v;
+  asm volatile("ld.shared::cluster.v4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+// Bounded wait with cluster-scope acquire (for phases completed by remote arrives).
+__device__ __forceinline__ bool mbar_test_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (TMA stores, tcgen05.mma operand reads).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // ------------------------------------------------------------------ tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -182,20 +233,26 @@ __host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
   return (1u << 4) | (0u << 7) | (0u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
 }
 
-// Shared-memory matrix descriptor for a K-major operand tile stored with the
-// 128-byte swizzle (rows of 128 bytes, 8-row / 1024-byte swizzle atoms), the
-// layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B.
+// Shared-memory matrix descriptor for a K-major operand tile stored with a
+// 128-byte or 64-byte swizzle (rows of 128 / 64 bytes, 8-row swizzle atoms of
+// 1024 / 512 bytes), the layouts TMA writes with CU_TENSOR_MAP_SWIZZLE_128B /
+// _64B.
 //   [0,14) start >> 4   [16,30) LBO >> 4 (unused for swizzled K-major: 1)
-//   [32,46) SBO >> 4 (1024 B between 8-row groups)   [46,48) version = 1
-//   [61,64) layout: 2 = SWIZZLE_128B
-__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t smem_addr) {
+//   [32,46) SBO >> 4 (bytes between 8-row groups)   [46,48) version = 1
+//   [61,64) layout: 2 = SWIZZLE_128B, 4 = SWIZZLE_64B
+template <int RowBytes>
+__device__ __forceinline__ uint64_t sdesc_kmajor(uint32_t smem_addr) {
+  static_assert(RowBytes == 128 || RowBytes == 64, "row bytes");
   uint64_t d = 0;
   d |= uint64_t((smem_addr >> 4) & 0x3FFF);
   d |= uint64_t(1) << 16;
-  d |= uint64_t(1024 >> 4) << 32;
+  d |= uint64_t((8 * RowBytes) >> 4) << 32;
   d |= uint64_t(1) << 46;
-  d |= uint64_t(2) << 61;
+  d |= uint64_t(RowBytes == 128 ? 2 : 4) << 61;
   return d;
+}
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t smem_addr) {
+  return sdesc_kmajor<128>(smem_addr);
 }
 
 // TMEM loads/stores, 32 lanes x 32 bit shape: thread i of the warp accesses
@@ -217,6 +274,35 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* v) {
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* v) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      PB2_W8(v, 0), PB2_W8(v, 8), PB2_W8(v, 16), PB2_W8(v, 24)
+      : "memory");
+}
+#undef PB2_W8
+
+// TMEM loads/stores, 16 lanes x 256 bit shape, 8 repetitions (64 columns):
+// thread t holds, for repetition j, (lane base + t/4, col 8j + 2(t%4)),
+// (lane base + t/4, col 8j + 2(t%4) + 1), (lane base + t/4 + 8, same two
+// cols) in registers 4j..4j+3 -- the per-thread fragment of a protocol hash
+// tile (rows r, r+8; column class t%4).
+#define PB2_R8(p, o) "=r"(p[o + 0]), "=r"(p[o + 1]), "=r"(p[o + 2]), "=r"(p[o + 3]), \
+    "=r"(p[o + 4]), "=r"(p[o + 5]), "=r"(p[o + 6]), "=r"(p[o + 7])
+__device__ __forceinline__ void tmem_ld16x256_x8(uint32_t taddr, uint32_t* v) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x8.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : PB2_R8(v, 0), PB2_R8(v, 8), PB2_R8(v, 16), PB2_R8(v, 24)
+      : "r"(taddr)
+      : "memory");
+}
+#undef PB2_R8
+#define PB2_W8(p, o) "r"(p[o + 0]), "r"(p[o + 1]), "r"(p[o + 2]), "r"(p[o + 3]), \
+    "r"(p[o + 4]), "r"(p[o + 5]), "r"(p[o + 6]), "r"(p[o + 7])
+__device__ __forceinline__ void tmem_st16x256_x8(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x256b.x8.b32 [%0], "
       "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
       "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
       PB2_W8(v, 0), PB2_W8(v, 8), PB2_W8(v, 16), PB2_W8(v, 24)
