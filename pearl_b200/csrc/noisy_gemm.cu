@@ -1,51 +1,60 @@
 // noisy_gemm.cu -- the mined GEMM on sm_100a tensor cores.
 //
-// One CTA computes a 128 x 256 output tile S = ApEA . BpEB^T (int8 x int8 ->
-// int32) with tcgen05.mma; the accumulator lives in 256 TMEM columns, so two
-// CTAs share an SM and the tensor core alternates between them.  Operand tiles
-// (128 bytes of K per stage, 128-byte swizzle) stream in by TMA.
+// A cluster of two CTAs (one per SM) computes 256 x 256 output tiles with
+// 2-SM MMAs (tcgen05.mma.cta_group::2, int8 x int8 -> int32): each CTA loads
+// 128 rows of ApEA and half of the 256 BpEB rows per K stage, so an SM streams
+// 32 KB per 128 bytes of K and the leader CTA issues one M=256, N=256 MMA per
+// 32 bytes of K.  Each CTA's tensor memory (512 columns) holds its 128 x 256
+// half of two independent tiles ("slots"); the leader issues the slots'
+// R-chunks of K in strict alternation, so while the tensor core runs one
+// slot's chunk the epilogue reads the other slot's running accumulator for
+// the transcript -- the MMA does not wait for a fold.
 //
 // Transcript (protocol: zk-pow/src/ffi/mine.rs:86-107; GPU twin
-// pearl-gemm/csrc/gemm/pow_utils.hpp:129-200 and collective_mainloop.hpp:270-317):
-// every R steps of K the MMA warp commits, the four epilogue warps read the
-// running accumulator from TMEM (thread = row), XOR each row's 256 values into
-// four column classes ((col / 2) % 4), pair rows r and r + 8 with one shuffle
-// and rotate-xor the result into word (chunk % 16) of the 16-word transcript of
-// each 2 x 64 protocol hash tile (rows {r, r+8} x cols {c + 8j, c + 8j + 1}).
-// Each epilogue thread owns two hash tiles.  The fold and the rotate-xor are
-// GF(2)-linear, so folding the two rows separately and XOR-ing is exact.
-//
+// pearl-gemm/csrc/gemm/pow_utils.hpp:129-200, collective_mainloop.hpp:270-317):
+// after each R-chunk a slot's accumulator is read by 16 fold warps (4 per
+// TMEM lane quadrant, 64 columns each, 32x32b loads) and XOR-folded onto the
+// protocol's 2 x 64 hash tiles (rows {r, r+8} x cols {c + 8j, c + 8j + 1});
+// one thread per hash tile rotate-xors the folded word into word (chunk % 16)
+// of the tile's register transcript.  Fold and rotate-xor are GF(2)-linear,
+// so the per-strip partial folds simply XOR together.  Reading 128 KB of TMEM
+// per chunk at full MMA rate needs ~256 B/cycle per SM; 16 warps of 32x32b
+// loads deliver ~470.
+
 // Epilogue (collective_epilogue.hpp:361-599 semantics): the final int32
-// accumulator is rewritten in TMEM as f32 * 2^-12, two f16 MMAs add the
+// accumulator is rewritten in TMEM as f32 * 2^-12, f16 2-SM MMAs add the
 // low-rank denoise terms EAL_fp16 . EARxBpEB_fp16^T + AxEBL_fp16 . EBR_fp16^T,
-// and C = bf16(D * 2^12 * A_scales[m] * B_scales[n]) is stored.  Each hash
-// tile's transcript is hashed with keyed BLAKE3 (pow_utils.hpp:205-234) and
-// compared with the uint256 target; hits are published without any spin
-// lock (first hit claims the pinned host header with one atomicCAS).
+// and C = bf16(D * 2^12 * A_scales[m] * B_scales[n]) is stored.  Two hash
+// warps per CTA combine the partial transcripts, hash each tile with keyed
+// BLAKE3 (pow_utils.hpp:205-234) and compare with the uint256 target; hits
+// are published without any spin lock (the first hit claims the pinned host
+// header with one atomicCAS).
 #include <cuda_bf16.h>
 
 #include <algorithm>
 #include <cstring>
+#include <type_traits>
 
 #include "pb2_common.cuh"
 
 namespace pb2 {
 namespace {
 
-constexpr int BM = 128;
+constexpr int BMC = 128;     // rows per CTA (half of the pair tile)
+constexpr int BM = 2 * BMC;  // rows per pair tile
 constexpr int BN = 256;
-constexpr int BK = 128;  // bytes of K per pipeline stage (one 128-byte swizzle row)
-constexpr int kStages = 2;
-constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 epilogue
-constexpr int kAStage = BM * BK;
-constexpr int kBStage = BN * BK;
-constexpr int kStageBytes = kAStage + kBStage;
-constexpr int kTmemCols = 256;
-constexpr uint32_t kIdescI8 = idesc_i8(BM, BN);
-constexpr uint32_t kIdescF16 = idesc_f16(BM, BN);
+constexpr int kTileK = 128;  // the reference's tile_size_k (K must be a multiple)
+constexpr int kFoldWarps = 16;
+constexpr int kThreads = 32 * (2 + kFoldWarps);  // TMA, MMA, fold
+constexpr int kStageBudget = 160 * 1024;                       // operand ring bytes
+constexpr int kMaxStages = 8;
+constexpr int kXbufBytes = 2 * 16 * 256 * 4;                   // transcripts of 256 hash tiles per slot
+constexpr int kFbufBytes = 2 * kFoldWarps * 64 * 4;            // posted fold values, 2 buffers
+constexpr int kTmemCols = 512;
+constexpr uint16_t kPairMask = 0x3;
 
 struct MainArgs {
-  CUtensorMap tmA, tmB;      // ApEA (m,k), BpEB (n,k): int8
+  CUtensorMap tmA, tmB;      // ApEA (m,k), BpEB (n,k): int8, boxes of 128 rows
   CUtensorMap tmDA0, tmDB0;  // EAL_fp16 (m,r), EARxBpEB_fp16 (n,r)
   CUtensorMap tmDA1, tmDB1;  // AxEBL_fp16 (m,r), EBR_fp16 (n,r)
   int M, N, K, R;
@@ -65,10 +74,10 @@ struct MainArgs {
 };
 
 struct Smem {
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
-  uint64_t acc_full;
-  uint64_t acc_empty;
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -83,6 +92,9 @@ __device__ __forceinline__ void tile_coords(const MainArgs& a, int t, int& tm, i
   tm = first_m + within % gm;
   tn = within / gm;
 }
+
+// Per-slot phase bits packed in one word (bit s = parity of slot s).
+__device__ __forceinline__ uint32_t bit(uint32_t w, int s) { return (w >> s) & 1u; }
 
 __device__ __forceinline__ uint32_t pack_bf16(float x, float y) {
   __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
@@ -113,29 +125,19 @@ __device__ __forceinline__ void store_c32(const MainArgs& a, const uint32_t* v, 
   }
 }
 
-// Rotate-xor `f` into word (chunk % 16) of a register-resident transcript.
-__device__ __forceinline__ void transcript_update(uint32_t* T, int chunk, uint32_t f) {
-  switch (chunk & 15) {
-#define PB2_TU(i) \
-  case i:         \
-    T[i] = rotl13(T[i]) ^ f; \
-    break;
-    PB2_TU(0) PB2_TU(1) PB2_TU(2) PB2_TU(3) PB2_TU(4) PB2_TU(5) PB2_TU(6) PB2_TU(7)
-    PB2_TU(8) PB2_TU(9) PB2_TU(10) PB2_TU(11) PB2_TU(12) PB2_TU(13) PB2_TU(14) PB2_TU(15)
-#undef PB2_TU
-  }
-}
-
-__device__ void publish_hit(const MainArgs& a, int tm, int tn, int row_in_tile, int cls,
+// Hit publication.  Rows are reported in the reference's 128-row tile
+// convention (tileCoord[0] = 128-row block, thread rows < 128), so
+// extract_indices() gives the same A rows as for the reference kernel.
+__device__ void publish_hit(const MainArgs& a, int tm128, int tn, int row_in_tile, int cls,
                             const uint32_t* digest) {
-  const uint32_t row_off = uint32_t(tm * BM + row_in_tile);
+  const uint32_t row_off = uint32_t(tm128 * BMC + row_in_tile);
   const uint32_t col_off = uint32_t(tn * BN + 2 * cls);
   const unsigned slot = atomicAdd(&a.sync->hit_count, 1u);
   if (a.hits && (long long)slot < a.hit_cap) {
     uint32_t* h = a.hits + size_t(slot) * PB2_HIT_WORDS;
     h[0] = row_off;
     h[1] = col_off;
-    h[2] = uint32_t(tm);
+    h[2] = uint32_t(tm128);
     h[3] = uint32_t(tn);
 #pragma unroll
     for (int i = 0; i < 8; ++i) h[4 + i] = digest[i];
@@ -145,7 +147,7 @@ __device__ void publish_hit(const MainArgs& a, int tm, int tn, int row_in_tile, 
     H->gridDim[0] = gridDim.x; H->gridDim[1] = gridDim.y; H->gridDim[2] = gridDim.z;
     H->blockDim[0] = blockDim.x; H->blockDim[1] = blockDim.y; H->blockDim[2] = blockDim.z;
     H->blockIdx[0] = blockIdx.x; H->blockIdx[1] = blockIdx.y; H->blockIdx[2] = blockIdx.z;
-    H->tileCoord[0] = uint32_t(tm); H->tileCoord[1] = uint32_t(tn); H->tileCoord[2] = 0;
+    H->tileCoord[0] = uint32_t(tm128); H->tileCoord[1] = uint32_t(tn); H->tileCoord[2] = 0;
     H->threadIdx[0] = threadIdx.x; H->threadIdx[1] = 0; H->threadIdx[2] = 0;
     H->num_registers_per_thread = 128;
     // Element j of the hash tile, in the reference's per-thread fragment
@@ -155,7 +157,7 @@ __device__ void publish_hit(const MainArgs& a, int tm, int tn, int row_in_tile, 
       H->thread_cols[j] = uint8_t(2 * cls + (j & 1) + 8 * (j >> 2));
     }
     H->mma_size[0] = a.M; H->mma_size[1] = a.N; H->mma_size[2] = a.K;
-    H->mma_tile_size[0] = BM; H->mma_tile_size[1] = BN; H->mma_tile_size[2] = BK;
+    H->mma_tile_size[0] = BMC; H->mma_tile_size[1] = BN; H->mma_tile_size[2] = kTileK;
     for (int i = 0; i < 8; ++i) H->target[i] = a.target[i];
     __threadfence_system();
     H->status = 1;
@@ -164,26 +166,45 @@ __device__ void publish_hit(const MainArgs& a, int tm, int tn, int row_in_tile, 
   }
 }
 
-template <bool kReduce, bool kDenoise, bool kDebug>
-__global__ void __launch_bounds__(kThreads, 2) noisy_gemm_kernel(const __grid_constant__ MainArgs a) {
+template <int BK, bool kReduce, bool kDenoise, bool kDebug>
+__global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_constant__ MainArgs a) {
+  constexpr int kAStage = BMC * BK;        // this CTA's 128 rows of A
+  constexpr int kBStage = (BN / 2) * BK;   // this CTA's half of the 256 rows of B
+  constexpr int kStageBytes = kAStage + kBStage;
+  constexpr int kStages =
+      (kStageBudget / kStageBytes) < kMaxStages ? (kStageBudget / kStageBytes) : kMaxStages;
+  constexpr uint32_t kIdescI8 = idesc_i8(BM, BN);
+  constexpr uint32_t kIdescF16 = idesc_f16(BM, BN);
+
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_mem = base;
-  Smem& S = *reinterpret_cast<Smem*>(base + kStages * kStageBytes);
+  uint32_t* xbuf = reinterpret_cast<uint32_t*>(base + kStageBudget);
+  uint32_t* fbuf = reinterpret_cast<uint32_t*>(base + kStageBudget + kXbufBytes);
+  Smem& S = *reinterpret_cast<Smem*>(base + kStageBudget + (kReduce ? kXbufBytes + kFbufBytes : 0));
   volatile int* abort_flag = &S.abort_flag;
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int nkb = a.K / BK;
-  const int nden = kDenoise ? 2 * (a.R / 64) : 0;
+  const uint32_t rank = cluster_ctarank();  // 0 = leader (issues the MMAs), 1 = peer
+  // A unit is one R-chunk of K (the transcript period) of one tile; without
+  // transcript and denoise the chunk length only sets the interleaving.
+  const int unit_k = (kReduce || kDenoise) ? a.R : kTileK;
+  const int stages_per_unit = unit_k / BK;
+  const int nmain = a.K / unit_k;
+  const int nden = kDenoise ? 4 : 0;  // 2 products x 2R bytes of fp16 K = 4 units of R bytes
+  const int units = nmain + nden;
+  const int den_stages_per_product = 2 * a.R / BK;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&S.full[i], 1);
       mbar_init(&S.empty[i], 1);
     }
-    mbar_init(&S.acc_full, 1);
-    mbar_init(&S.acc_empty, 4);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&S.acc_full[i], 1);
+      mbar_init(&S.acc_empty[i], 2 * kFoldWarps);  // both CTAs' fold warps release a slot
+    }
     mbar_init(&S.drain, 1);
     S.abort_flag = 0;
     fence_barrier_init();
@@ -197,230 +218,348 @@ __global__ void __launch_bounds__(kThreads, 2) noisy_gemm_kernel(const __grid_co
     }
   }
   if (warp == 1) {
-    tmem_alloc(&S.tmem_base, kTmemCols);
-    tmem_relinquish();
+    tmem_alloc_2sm(&S.tmem_base, kTmemCols);
+    tmem_relinquish_2sm();
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any remote arrive or 2-SM load
   tc_fence_after();
   const uint32_t tmem = S.tmem_base;
+
+  // Pair tiles are processed in rounds: round r holds tiles t0 = first + r *
+  // stride (slot 0) and t0 + 1 (slot 1, when it exists); within a round the
+  // units alternate slot 0, slot 1.  Every role walks this order.
+  const int first = 2 * int(blockIdx.x >> 1);
+  const int stride = int(gridDim.x);
+  using I0 = std::integral_constant<int, 0>;
+  using I1 = std::integral_constant<int, 1>;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       uint32_t it = 0;
-      for (int t = blockIdx.x; t < a.num_tiles && !*abort_flag; t += gridDim.x) {
-        int tm, tn;
-        tile_coords(a, t, tm, tn);
-        const int m0 = tm * BM, n0 = tn * BN;
-        for (int kb = 0; kb < nkb + nden; ++kb, ++it) {
-          const int s = it % kStages;
-          if (!mbar_wait(&S.empty[s], ((it / kStages) & 1) ^ 1, abort_flag, a.sync)) break;
-          mbar_arrive_expect_tx(&S.full[s], kStageBytes);
-          uint8_t* sa = stage_mem + s * kStageBytes;
-          uint8_t* sb = sa + kAStage;
-          if (kb < nkb) {
-            tma_load_2d(&a.tmA, &S.full[s], sa, kb * BK, m0);
-            tma_load_2d(&a.tmB, &S.full[s], sb, kb * BK, n0);
-          } else {
-            const int d = kb - nkb;
-            const int per = a.R / 64;
-            const int col = (d % per) * 64;
-            const bool second = d >= per;
-            tma_load_2d(second ? &a.tmDA1 : &a.tmDA0, &S.full[s], sa, col, m0);
-            tma_load_2d(second ? &a.tmDB1 : &a.tmDB0, &S.full[s], sb, col, n0);
+      bool ok = true;
+      for (int t0 = first; t0 < a.num_tiles && ok; t0 += stride) {
+        const bool two = t0 + 1 < a.num_tiles;
+        int tm0, tn0, tm1 = 0, tn1 = 0;
+        tile_coords(a, t0, tm0, tn0);
+        if (two) tile_coords(a, t0 + 1, tm1, tn1);
+        // This CTA's 128 rows of A and half of the B rows, per slot.
+        const int ma = tm0 * BM + int(rank) * BMC, na = tn0 * BN + int(rank) * (BN / 2);
+        const int mb = tm1 * BM + int(rank) * BMC, nb = tn1 * BN + int(rank) * (BN / 2);
+        for (int u = 0; u < units && ok; ++u) {
+          for (int s = 0; s < (two ? 2 : 1) && ok; ++s) {
+            const int m0 = s ? mb : ma, n0 = s ? nb : na;
+            for (int st = 0; st < stages_per_unit; ++st, ++it) {
+              const int j = it % kStages;
+              if (!(ok = mbar_wait(&S.empty[j], ((it / kStages) & 1) ^ 1, abort_flag, a.sync))) break;
+              // The leader's full barrier counts both CTAs' bytes.
+              if (rank == 0) mbar_arrive_expect_tx(&S.full[j], 2 * kStageBytes);
+              uint8_t* sa = stage_mem + j * kStageBytes;
+              uint8_t* sb = sa + kAStage;
+              if (u < nmain) {
+                const int kbyte = u * unit_k + st * BK;
+                tma_load_2d_2sm(&a.tmA, &S.full[j], sa, kbyte, m0);
+                tma_load_2d_2sm(&a.tmB, &S.full[j], sb, kbyte, n0);
+              } else {
+                const int d = (u - nmain) * stages_per_unit + st;
+                const bool second = d >= den_stages_per_product;
+                const int col = (d % den_stages_per_product) * (BK / 2);
+                tma_load_2d_2sm(second ? &a.tmDA1 : &a.tmDA0, &S.full[j], sa, col, m0);
+                tma_load_2d_2sm(second ? &a.tmDB1 : &a.tmDB0, &S.full[j], sb, col, n0);
+              }
+            }
           }
         }
       }
-      // Drain: wait (bounded) until every issued stage has landed before exit.
-      for (uint32_t j = (it > kStages ? it - kStages : 0); j < it; ++j) {
+      // Drain (bounded): every issued stage has been consumed by the MMAs,
+      // hence has landed, before this CTA leaves.
+      for (uint32_t j = (it > uint32_t(kStages) ? it - kStages : 0); j < it; ++j) {
         long long t0 = clock64();
-        while (!mbar_test(&S.full[j % kStages], (j / kStages) & 1) && clock64() - t0 < 100000000LL) {
+        while (!mbar_test(&S.empty[j % kStages], (j / kStages) & 1) && clock64() - t0 < 100000000LL) {
         }
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    // The issuing thread's instruction stream is kept lean: the i8 and f16
+    // MMAs sit in separate loops and the accumulate flag is computed once per
+    // stage (a runtime kind switch inside the unrolled MMA block measurably
+    // slows the issue rate below the tensor pipe's).
+    if (lane == 0 && rank == 0) {
       uint32_t it = 0;
-      uint32_t acc_parity = 0;
-      bool pending = false;  // an acc_full commit still awaits the epilogue's release
+      uint32_t empar = 0;  // acc_empty parity per slot
+      uint32_t pend = 0;   // bit s: an acc_full commit of slot s awaits the fold warps' release
       bool ok = true;
       const uint32_t sbase = smem_u32(stage_mem);
-      for (int t = blockIdx.x; t < a.num_tiles && ok; t += gridDim.x) {
-        for (int kb = 0; kb < nkb + nden && ok; ++kb, ++it) {
-          const int s = it % kStages;
-          if (!(ok = mbar_wait(&S.full[s], (it / kStages) & 1, abort_flag, a.sync))) break;
+      auto acquire = [&](int s) -> bool {
+        if (!bit(pend, s)) return true;
+        if (!mbar_wait(&S.acc_empty[s], bit(empar, s), abort_flag, a.sync)) return false;
+        empar ^= 1u << s;
+        pend &= ~(1u << s);
+        tc_fence_after();
+        return true;
+      };
+      auto main_unit = [&](int s, int u) {
+        if ((kReduce || u == 0) && !(ok = acquire(s))) return;
+        const uint32_t dt = tmem + 256 * s;
+        for (int st = 0; st < stages_per_unit; ++st, ++it) {
+          const int j = it % kStages;
+          if (!(ok = mbar_wait(&S.full[j], (it / kStages) & 1, abort_flag, a.sync))) return;
           tc_fence_after();
-          const uint64_t ad = sdesc_sw128(sbase + s * kStageBytes);
-          const uint64_t bd = sdesc_sw128(sbase + s * kStageBytes + kAStage);
+          const uint64_t ad = sdesc_kmajor<BK>(sbase + j * kStageBytes);
+          const uint64_t bd = sdesc_kmajor<BK>(sbase + j * kStageBytes + kAStage);
+          umma_i8_2sm(dt, ad, bd, kIdescI8, uint32_t((u | st) != 0));
 #pragma unroll
-          for (int ks = 0; ks < BK / 32; ++ks) {
-            if (pending) {
-              if (!(ok = mbar_wait(&S.acc_empty, acc_parity, abort_flag, a.sync))) break;
-              acc_parity ^= 1;
-              pending = false;
-              tc_fence_after();
-            }
-            if (kb < nkb) {
-              umma_i8(tmem, ad + 2 * ks, bd + 2 * ks, kIdescI8, (kb | ks) != 0);
-              if (kReduce && ((kb * BK + (ks + 1) * 32) % a.R) == 0) {
-                umma_commit(&S.acc_full);
-                pending = true;
-              }
-            } else {
-              umma_f16(tmem, ad + 2 * ks, bd + 2 * ks, kIdescF16, 1);
-            }
-          }
-          if (!ok) break;
-          umma_commit(&S.empty[s]);
-          // End of the main loop without transcript: hand the accumulator over.
-          if (!kReduce && kb == nkb - 1) {
-            umma_commit(&S.acc_full);
-            pending = true;
-          }
-          if (kDenoise && kb == nkb + nden - 1) {
-            umma_commit(&S.acc_full);
-            pending = true;
+          for (int ks = 1; ks < BK / 32; ++ks) umma_i8_2sm(dt, ad + 2 * ks, bd + 2 * ks, kIdescI8, 1);
+          umma_commit_2sm(&S.empty[j], kPairMask);
+        }
+        if (kReduce || u == nmain - 1) {
+          umma_commit_2sm(&S.acc_full[s], kPairMask);
+          pend |= 1u << s;
+        }
+      };
+      auto denoise_unit = [&](int s, int d) {
+        if (d == 0 && !(ok = acquire(s))) return;  // S has been rewritten as f32
+        const uint32_t dt = tmem + 256 * s;
+        for (int st = 0; st < stages_per_unit; ++st, ++it) {
+          const int j = it % kStages;
+          if (!(ok = mbar_wait(&S.full[j], (it / kStages) & 1, abort_flag, a.sync))) return;
+          tc_fence_after();
+          const uint64_t ad = sdesc_kmajor<BK>(sbase + j * kStageBytes);
+          const uint64_t bd = sdesc_kmajor<BK>(sbase + j * kStageBytes + kAStage);
+#pragma unroll
+          for (int ks = 0; ks < BK / 32; ++ks) umma_f16_2sm(dt, ad + 2 * ks, bd + 2 * ks, kIdescF16, 1);
+          umma_commit_2sm(&S.empty[j], kPairMask);
+        }
+        if (d == nden - 1) {
+          umma_commit_2sm(&S.acc_full[s], kPairMask);
+          pend |= 1u << s;
+        }
+      };
+      for (int t0 = first; t0 < a.num_tiles && ok; t0 += stride) {
+        const bool two = t0 + 1 < a.num_tiles;
+        for (int u = 0; u < nmain && ok; ++u) {
+          main_unit(0, u);
+          if (two && ok) main_unit(1, u);
+        }
+        if (kDenoise) {
+          for (int d = 0; d < nden && ok; ++d) {
+            denoise_unit(0, d);
+            if (two && ok) denoise_unit(1, d);
           }
         }
       }
-      // Make sure every MMA has retired before TMEM is released.
-      umma_commit(&S.drain);
+      // Every MMA has retired before TMEM is released.
+      umma_commit_2sm(&S.drain, 0x1);
       long long t0 = clock64();
       while (!mbar_test(&S.drain, 0) && clock64() - t0 < 100000000LL) {
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
-    const int row_in_tile = 32 * q + lane;
-    const uint32_t trow = tmem + (uint32_t(32 * q) << 16);
+    // ------------------------------------------------------------ fold warps
+    // Four warps per TMEM lane quadrant q = warp % 4 (the quadrant a warp may
+    // access); warp index wi = 0..3 within the quadrant picks the 64-column
+    // strip [64 wi, 64 wi + 64).  Loads use the 32x32b shape (thread = row),
+    // which reads TMEM about twice as fast as the 16-lane shapes; both
+    // 32-column loads of a strip are in flight before the wait.
+    //
+    // Fold of one R-chunk: each thread XORs its row's strip values into the
+    // four column classes (col / 2) % 4 of the hash tiles, pairs rows r and
+    // r + 8 with one shuffle (lanes with bit 3 clear keep classes 0 and 1,
+    // their partners 2 and 3), and posts the two values to shared memory.
+    // After a barrier of the quadrant's 128 threads, lane p < 16 of warp wi
+    // owns hash tile (row pair p, class wi) = tile q * 64 + wi * 16 + p: it
+    // XORs the four strips' values and rotate-xors the result into word
+    // (chunk % 16) of the tile's transcript in shared memory.  After the last
+    // chunk the owner hashes the transcript.  The quadrant's 16 row pairs are
+    // rows 32 q + (p % 8) + 16 (p / 8) and +8.
+    const int fw = warp - 2;
+    const int q = warp & 3;
+    const int wi = fw >> 2;
     const bool is_low = (lane & 8) == 0;
-    const int cls0 = is_low ? 0 : 2;
-    const int tile_row = 32 * q + (lane & ~8);  // first row of this thread's hash tiles
-    const int nchunks = kReduce ? a.K / a.R : 0;
-    uint32_t acc_parity = 0;
+    const uint32_t strip_off = (uint32_t(32 * q) << 16) + 64 * wi;
+    // Slot releases go to the leader's acc_empty (remotely from the peer).
+    const uint32_t rel_base = mapa(&S.acc_empty[0], 0);
+    // Owner lane p reads the posted values of lane src (word cls & 1) of
+    // each strip warp of the quadrant.
+    const int own_p = lane & 15;
+    const int own_src = (own_p & 7) + 16 * (own_p >> 3) + (wi >= 2 ? 8 : 0);
+    const int own_word = wi & 1;
+    const int own_tile = q * 64 + wi * 16 + own_p;
+    const int own_row = 32 * q + (own_p & 7) + 16 * (own_p >> 3);
+    uint32_t fpar = 0;    // acc_full parity per slot
+    uint32_t events = 0;  // fold events so far (selects the posting buffer)
     bool ok = true;
 
-    for (int t = blockIdx.x; t < a.num_tiles && ok; t += gridDim.x) {
-      int tm, tn;
-      tile_coords(a, t, tm, tn);
-      const int64_t row = int64_t(tm) * BM + row_in_tile;
-      const int n0 = tn * BN;
-      const float sa = row < a.M ? a.sA[row] : 0.0f;
-      uint32_t T0[16], T1[16];
+    auto fold_slot = [&](auto slot, int u, int tm, int tn) {
+      constexpr int s = decltype(slot)::value;
+      const bool is_main = u < nmain;
+      const bool last_main = u == nmain - 1;
+      if (!(ok = mbar_wait(&S.acc_full[s], bit(fpar, s), abort_flag, a.sync))) return;
+      fpar ^= 1u << s;
+      tc_fence_after();
+      const uint32_t taddr = tmem + 256 * s + strip_off;
+      const bool do_fold = kReduce && is_main;
+      const bool do_convert = kDenoise && last_main;
+      const bool do_store = (!kDenoise && last_main) || !is_main;
+      uint32_t v[64];
+      __syncwarp();
+      tmem_ld32(taddr, v);
+      tmem_ld32(taddr + 32, v + 32);
+      tmem_wait_ld();
+      uint32_t p0 = 0, p1 = 0, p2 = 0, p3 = 0;
+      if (do_fold) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) T0[i] = T1[i] = 0;
-
-      // Sync points of this tile: one per transcript chunk (or one at the end
-      // without transcript), plus one after the denoise MMAs.
-      const int nsync = (kReduce ? nchunks : 1) + (kDenoise ? 1 : 0);
-      for (int sp = 0; sp < nsync; ++sp) {
-        if (!(ok = mbar_wait(&S.acc_full, acc_parity, abort_flag, a.sync))) break;
-        acc_parity ^= 1;
-        tc_fence_after();
-        const bool denoised = kDenoise && sp == nsync - 1;   // D is f32, final
-        const bool fold = kReduce && !denoised;
-        const bool last_int = !denoised && sp == (kReduce ? nchunks : 1) - 1;
-        uint32_t p0 = 0, p1 = 0, p2 = 0, p3 = 0;
-#pragma unroll 1
-        for (int b = 0; b < BN / 32; b += 2) {
-          uint32_t v[64];
-          __syncwarp();  // tcgen05.ld/st are .sync.aligned: reconverge after per-lane stores
-          tmem_ld32(trow + 32 * b, v);
-          tmem_ld32(trow + 32 * b + 32, v + 32);
-          tmem_wait_ld();
-          if (fold) {
-#pragma unroll
-            for (int i = 0; i < 64; i += 8) {
-              p0 ^= v[i] ^ v[i + 1];
-              p1 ^= v[i + 2] ^ v[i + 3];
-              p2 ^= v[i + 4] ^ v[i + 5];
-              p3 ^= v[i + 6] ^ v[i + 7];
-            }
-          }
-          if (denoised) {
-            store_c32<true>(a, v, row, n0 + 32 * b, sa * 4096.0f);
-            store_c32<true>(a, v + 32, row, n0 + 32 * b + 32, sa * 4096.0f);
-          } else if (last_int) {
-            if (kDenoise) {
-              // rewrite S as f32 * 2^-12 for the f16 denoise MMAs
-#pragma unroll
-              for (int i = 0; i < 64; ++i) v[i] = __float_as_uint(float(int(v[i])) * (1.0f / 4096.0f));
-              tmem_st32(trow + 32 * b, v);
-              tmem_st32(trow + 32 * b + 32, v + 32);
-            } else {
-              store_c32<false>(a, v, row, n0 + 32 * b, sa);
-              store_c32<false>(a, v + 32, row, n0 + 32 * b + 32, sa);
-            }
-          }
+        for (int i = 0; i < 64; i += 8) {
+          p0 ^= v[i] ^ v[i + 1];
+          p1 ^= v[i + 2] ^ v[i + 3];
+          p2 ^= v[i + 4] ^ v[i + 5];
+          p3 ^= v[i + 6] ^ v[i + 7];
         }
-        if (fold) {
-          const uint32_t s0 = is_low ? p2 : p0, s1 = is_low ? p3 : p1;
-          const uint32_t r0 = __shfl_xor_sync(0xffffffffu, s0, 8);
-          const uint32_t r1 = __shfl_xor_sync(0xffffffffu, s1, 8);
-          const uint32_t f0 = (is_low ? p0 : p2) ^ r0;
-          const uint32_t f1 = (is_low ? p1 : p3) ^ r1;
-          transcript_update(T0, sp, f0);
-          transcript_update(T1, sp, f1);
-          if (kDebug && lane == 0) atomicAdd(a.counter, 64ull);
-        }
-        __syncwarp();
-        if (kDenoise && last_int) tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&S.acc_empty);
       }
-      if (!ok) break;
-
-      if (kReduce) {
-        uint32_t key[8], tgt[8];
+      if (do_convert) {
+        // S as f32 * 2^-12 for the f16 denoise MMAs.
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          key[i] = a.key[i];
-          tgt[i] = a.target[i];
+        for (int i = 0; i < 64; ++i) v[i] = __float_as_uint(float(int(v[i])) * (1.0f / 4096.0f));
+        tmem_st32(taddr, v);
+        tmem_st32(taddr + 32, v + 32);
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster_addr(rel_base + 8 * s);
+      if (do_store) {
+        const int64_t row = int64_t(tm) * BM + int(rank) * BMC + 32 * q + lane;
+        const float sa = row < a.M ? a.sA[row] : 0.0f;
+        if (!is_main) {
+          store_c32<true>(a, v, row, tn * BN + 64 * wi, sa * 4096.0f);
+          store_c32<true>(a, v + 32, row, tn * BN + 64 * wi + 32, sa * 4096.0f);
+        } else {
+          store_c32<false>(a, v, row, tn * BN + 64 * wi, sa);
+          store_c32<false>(a, v + 32, row, tn * BN + 64 * wi + 32, sa);
         }
-        const int64_t grow = int64_t(tm) * BM + tile_row;
+      }
+      if (do_fold) {
+        const uint32_t g0 = __shfl_xor_sync(0xffffffffu, is_low ? p2 : p0, 8);
+        const uint32_t g1 = __shfl_xor_sync(0xffffffffu, is_low ? p3 : p1, 8);
+        uint32_t* fb = fbuf + (events & 1) * (kFoldWarps * 64) + q * 256;
+        fb[(wi * 32 + lane) * 2 + 0] = (is_low ? p0 : p2) ^ g0;
+        fb[(wi * 32 + lane) * 2 + 1] = (is_low ? p1 : p3) ^ g1;
+        named_barrier_sync(1 + q, 128);
+        ++events;
+        if (lane < 16) {
+          const uint32_t x = fb[(0 * 32 + own_src) * 2 + own_word] ^ fb[(1 * 32 + own_src) * 2 + own_word] ^
+                             fb[(2 * 32 + own_src) * 2 + own_word] ^ fb[(3 * 32 + own_src) * 2 + own_word];
+          // Transcript words start at zero for every tile: rotl13(0) ^ x = x.
+          uint32_t* tw = xbuf + s * (16 * 256) + (u & 15) * 256 + own_tile;
+          *tw = u < 16 ? x : (rotl13(*tw) ^ x);
+        }
+        // The reference counts one hash per 2 x 64 tile of each 128-row
+        // tile that starts inside M.
+        if (kDebug && lane == 0 && tm * BM + int(rank) * BMC < a.M) atomicAdd(a.counter, 16ull);
+        if (last_main && lane < 16) {
+          // Transcript complete: keyed BLAKE3 and the target compare.
+          const uint32_t* tr = xbuf + s * (16 * 256) + own_tile;
+          uint32_t T[16], key[8], tgt[8], dg[8];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t* T = h == 0 ? T0 : T1;
-          const int cls = cls0 + h;
-          uint32_t dg[8];
+          for (int w = 0; w < 16; ++w) T[w] = w < nmain ? tr[w * 256] : 0u;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            key[i] = a.key[i];
+            tgt[i] = a.target[i];
+          }
           b3_compress8(key, T, kB3SingleBlockKeyed, dg);
-          const int64_t gcol = int64_t(n0) + 2 * cls;
+          const int tm128 = 2 * tm + int(rank);
+          const int cls = wi;
+          const int64_t grow = int64_t(tm128) * BMC + own_row;
+          const int64_t gcol = int64_t(tn) * BN + 2 * cls;
           const bool in_bounds = (grow + 8 < a.M) && (gcol + 249 < a.N);
           if (in_bounds && (a.transcripts || a.digests)) {
             const int64_t idx = (grow / 16 * 8 + grow % 16) * (a.N / 64) + gcol / 256 * 4 + (gcol % 256) / 2;
             if (a.transcripts)
-              for (int i = 0; i < 16; ++i) a.transcripts[idx * 16 + i] = T[i];
+              for (int w = 0; w < 16; ++w) a.transcripts[idx * 16 + w] = T[w];
             if (a.digests)
-              for (int i = 0; i < 8; ++i) a.digests[idx * 8 + i] = dg[i];
+              for (int w = 0; w < 8; ++w) a.digests[idx * 8 + w] = dg[w];
           }
-          if (in_bounds && u256_le(dg, tgt)) publish_hit(a, tm, tn, tile_row, cls, dg);
+          if (in_bounds && u256_le(dg, tgt)) publish_hit(a, tm128, tn, own_row, cls, dg);
         }
+      }
+    };
+
+    for (int t0 = first; t0 < a.num_tiles && ok; t0 += stride) {
+      const bool two = t0 + 1 < a.num_tiles;
+      int tm0, tn0, tm1 = 0, tn1 = 0;
+      tile_coords(a, t0, tm0, tn0);
+      if (two) tile_coords(a, t0 + 1, tm1, tn1);
+      for (int u = 0; u < units && ok; ++u) {
+        const bool is_main = u < nmain;
+        const bool event = (is_main && (kReduce || u == nmain - 1)) || (!is_main && u == units - 1);
+        if (!event) continue;
+        fold_slot(I0{}, u, tm0, tn0);
+        if (two && ok) fold_slot(I1{}, u, tm1, tn1);
       }
     }
   }
 
+  // Neither CTA leaves while its peer can still address its barriers or TMEM.
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();
   tc_fence_after();
   if (warp == 1) {
     __syncwarp();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc_2sm(tmem, kTmemCols);
   }
 }
 
 // ------------------------------------------------------------------ host
-template <bool R_, bool D_, bool G_>
-int launch_variant(const MainArgs& a, int grid, cudaStream_t s) {
-  auto kern = noisy_gemm_kernel<R_, D_, G_>;
-  const int smem = kStages * kStageBytes + int(sizeof(Smem)) + 1024;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return launch_status();
-  kern<<<grid, kThreads, smem, s>>>(a);
+template <int BK, bool R_, bool D_, bool G_>
+int launch_variant(const MainArgs& a, int device, cudaStream_t s) {
+  auto kern = noisy_gemm_kernel<BK, R_, D_, G_>;
+  const int smem = kStageBudget + (R_ ? kXbufBytes + kFbufBytes : 0) + int(sizeof(Smem)) + 1024;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return launch_status();
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = size_t(smem);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // A persistent grid: as many CTA pairs as can be co-resident (SM pairs in
+  // one GPC), never more than half the tiles (each pair runs two slots).
+  static int cached_pairs[64] = {0};
+  int& resident = cached_pairs[device & 63];
+  if (resident == 0) {
+    cfg.gridDim = dim3(2, 1, 1);
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters <= 0) {
+      cudaGetLastError();
+      const int sms = sm_count(device);
+      clusters = (sms > 0 ? sms : 148) / 2;
+    }
+    resident = clusters;
+  }
+  const int pairs = std::max(1, std::min((a.num_tiles + 1) / 2, resident));
+  cfg.gridDim = dim3(unsigned(2 * pairs), 1, 1);
+  cudaLaunchKernelEx(&cfg, kern, a);
   return launch_status();
+}
+
+template <int BK>
+int launch_bk(const MainArgs& a, int device, bool reduce, bool denoise, bool debug, cudaStream_t s) {
+  if (reduce && denoise) return debug ? launch_variant<BK, true, true, true>(a, device, s)
+                                      : launch_variant<BK, true, true, false>(a, device, s);
+  if (reduce) return debug ? launch_variant<BK, true, false, true>(a, device, s)
+                           : launch_variant<BK, true, false, false>(a, device, s);
+  if (denoise) return launch_variant<BK, false, true, false>(a, device, s);
+  return launch_variant<BK, false, false, false>(a, device, s);
 }
 
 bool al16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
@@ -429,10 +568,10 @@ bool al16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
 
 int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStream_t s) {
   if (p.m <= 0 || p.n <= 0 || p.k <= 0) return PB2_ERR_INVALID_ARGUMENT;
-  if (p.tile_size_m != BM || p.tile_size_n != BN || p.tile_size_k != BK) return PB2_ERR_UNSUPPORTED_CONFIG;
+  if (p.tile_size_m != BMC || p.tile_size_n != BN || p.tile_size_k != kTileK) return PB2_ERR_UNSUPPORTED_CONFIG;
   if (p.cluster_size_m != 1 || p.cluster_size_n != 1) return PB2_ERR_UNSUPPORTED_CONFIG;
-  // pipeline_stages is a hint: the ring depth is fixed by the 2-CTA/SM layout.
-  if (p.k % BK != 0 || p.n % 8 != 0) return PB2_ERR_INVALID_ARGUMENT;
+  // pipeline_stages is a hint: the ring depth is fixed by the shared-memory plan.
+  if (p.k % kTileK != 0 || p.n % 8 != 0) return PB2_ERR_INVALID_ARGUMENT;
   if (p.m > INT32_MAX || p.n > INT32_MAX || p.k > INT32_MAX) return PB2_ERR_INVALID_ARGUMENT;
   if ((reduce || denoise) && !(p.r == 64 || p.r == 128 || p.r == 256)) return PB2_ERR_UNSUPPORTED_CONFIG;
   if ((reduce || denoise) && (p.k % p.r != 0)) return PB2_ERR_INVALID_ARGUMENT;
@@ -445,21 +584,24 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
   if (debug && !p.inner_hash_counter) return PB2_ERR_INVALID_ARGUMENT;
   if ((p.transcripts || p.digests) && (p.m % 16 != 0 || p.n % 256 != 0)) return PB2_ERR_INVALID_ARGUMENT;
 
+  // 128-byte stages (128-byte swizzle) unless R = 64, where 64-byte stages
+  // (64-byte swizzle) keep a transcript chunk a whole number of stages.
+  const int bk = ((reduce || denoise) && p.r == 64) ? 64 : 128;
+  const CUtensorMapSwizzle swz = bk == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   MainArgs a;
   std::memset(&a, 0, sizeof(a));
   int st;
-  if ((st = make_tmap_2d(&a.tmA, p.ApEA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.k, p.m, BK, BM,
-                         CU_TENSOR_MAP_SWIZZLE_128B)))
+  if ((st = make_tmap_2d(&a.tmA, p.ApEA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.k, p.m, bk, BMC, swz)))
     return st;
-  if ((st = make_tmap_2d(&a.tmB, p.BpEB, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.k, p.n, BK, BN,
-                         CU_TENSOR_MAP_SWIZZLE_128B)))
+  if ((st = make_tmap_2d(&a.tmB, p.BpEB, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.k, p.n, bk, BN / 2, swz)))
     return st;
   if (denoise) {
     const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    if ((st = make_tmap_2d(&a.tmDA0, p.EAL_fp16, F16, 2, p.r, p.m, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B)) ||
-        (st = make_tmap_2d(&a.tmDB0, p.EARxBpEB_fp16, F16, 2, p.r, p.n, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B)) ||
-        (st = make_tmap_2d(&a.tmDA1, p.AxEBL_fp16, F16, 2, p.r, p.m, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B)) ||
-        (st = make_tmap_2d(&a.tmDB1, p.EBR_fp16, F16, 2, p.r, p.n, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B)))
+    const int dc = bk / 2;  // fp16 elements per stage row
+    if ((st = make_tmap_2d(&a.tmDA0, p.EAL_fp16, F16, 2, p.r, p.m, dc, BMC, swz)) ||
+        (st = make_tmap_2d(&a.tmDB0, p.EARxBpEB_fp16, F16, 2, p.r, p.n, dc, BN / 2, swz)) ||
+        (st = make_tmap_2d(&a.tmDA1, p.AxEBL_fp16, F16, 2, p.r, p.m, dc, BMC, swz)) ||
+        (st = make_tmap_2d(&a.tmDB1, p.EBR_fp16, F16, 2, p.r, p.n, dc, BN / 2, swz)))
       return st;
   }
   a.M = int(p.m);
@@ -469,7 +611,7 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
   a.tiles_m = int((p.m + BM - 1) / BM);
   a.tiles_n = int((p.n + BN - 1) / BN);
   a.num_tiles = a.tiles_m * a.tiles_n;
-  a.group = p.swizzle > 0 ? p.swizzle : 16;
+  a.group = p.swizzle > 0 ? p.swizzle : 8;
   if (a.group > a.tiles_m) a.group = a.tiles_m;
   a.sA = p.A_scales;
   a.sB = p.B_scales;
@@ -484,14 +626,8 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
   a.transcripts = p.transcripts;
   a.digests = p.digests;
 
-  const int sms = sm_count(p.device);
-  const int grid = std::min(a.num_tiles, 2 * (sms > 0 ? sms : 148));
-  if (reduce && denoise) return debug ? launch_variant<true, true, true>(a, grid, s)
-                                      : launch_variant<true, true, false>(a, grid, s);
-  if (reduce) return debug ? launch_variant<true, false, true>(a, grid, s)
-                           : launch_variant<true, false, false>(a, grid, s);
-  if (denoise) return launch_variant<false, true, false>(a, grid, s);
-  return launch_variant<false, false, false>(a, grid, s);
+  return bk == 128 ? launch_bk<128>(a, p.device, reduce, denoise, debug, s)
+                   : launch_bk<64>(a, p.device, reduce, denoise, debug, s);
 }
 
 int denoise_convert(const int32_t* in, void* out, int64_t count, float scale, cudaStream_t s);

@@ -1,6 +1,6 @@
-// tmem_ld_bench.cu -- TMEM load microbenchmark: throughput of tcgen05.ld 32x32b.xN
-// with W warps per CTA, optionally with an MMA warp streaming into the other
-// half of TMEM.  One CTA per SM.
+// tmem_ld_bench.cu -- TMEM load microbenchmark: throughput of tcgen05.ld
+// 32x32b.xN and 16x256b.x8 with W warps per CTA, optionally with an MMA warp
+// streaming into the other half of TMEM.  One CTA per SM.
 #include <cstdio>
 #include <cstdlib>
 #include <vector>
@@ -8,13 +8,18 @@
 
 using namespace pb2;
 
-template <int X>
+// SHAPE 0: X columns of 32x32b (thread = lane); SHAPE 1: X / 32 loads of
+// 16x256b.x8 (16 lanes x 64 columns each, the same 4 KB per load per warp).
+template <int X, int SHAPE>
 __device__ __forceinline__ void ldx(uint32_t taddr, uint32_t* v) {
 #pragma unroll
-  for (int i = 0; i < X / 32; ++i) tmem_ld32(taddr + 32 * i, v + 32 * i);
+  for (int i = 0; i < X / 32; ++i) {
+    if (SHAPE == 0) tmem_ld32(taddr + 32 * i, v + 32 * i);
+    else tmem_ld16x256_x8(taddr + 64 * i, v + 32 * i);
+  }
 }
 
-template <int X>
+template <int X, int SHAPE>
 __global__ void bench(int iters, int mma_on, unsigned long long* out, uint32_t* sink) {
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ uint32_t tbase;
@@ -53,12 +58,13 @@ __global__ void bench(int iters, int mma_on, unsigned long long* out, uint32_t* 
     const int q = warp & 3;
     const int slot = warp / 4;  // spread warps over columns
     uint32_t acc = 0;
-    const uint32_t base = t + (uint32_t(32 * q) << 16) + (slot * X) % 256;
+    const uint32_t base = SHAPE == 0 ? t + (uint32_t(32 * q) << 16) + (slot * X) % 256
+                                     : t + (uint32_t(32 * q + 16 * (slot & 1)) << 16) + ((slot >> 1) * 2 * X) % 256;
     __syncwarp();
     long long t0 = clock64();
     for (int it = 0; it < iters; ++it) {
       uint32_t v[X];
-      ldx<X>(base, v);
+      ldx<X, SHAPE>(base, v);
       tmem_wait_ld();
 #pragma unroll
       for (int i = 0; i < X; ++i) acc ^= v[i];
@@ -73,7 +79,7 @@ __global__ void bench(int iters, int mma_on, unsigned long long* out, uint32_t* 
   if (warp == 0) { __syncwarp(); tmem_dealloc(t, 512); }
 }
 
-template <int X>
+template <int X, int SHAPE = 0>
 void run(int warps, int mma_on, int sms) {
   int threads = 32 * (warps + (mma_on ? 1 : 0));
   int iters = 2000;
@@ -81,8 +87,8 @@ void run(int warps, int mma_on, int sms) {
   cudaMalloc(&out, sizeof(unsigned long long) * sms * 65 + 64);
   cudaMalloc(&sink, sizeof(uint32_t) * sms * threads);
   cudaMemset(out, 0, sizeof(unsigned long long) * sms * 65 + 64);
-  cudaFuncSetAttribute(bench<X>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
-  bench<X><<<sms, threads, 100 * 1024>>>(iters, mma_on, out, sink);
+  cudaFuncSetAttribute(bench<X, SHAPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+  bench<X, SHAPE><<<sms, threads, 100 * 1024>>>(iters, mma_on, out, sink);
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) { printf("error %s\n", cudaGetErrorString(e)); exit(1); }
   std::vector<unsigned long long> h(sms * 65);
@@ -92,12 +98,21 @@ void run(int warps, int mma_on, int sms) {
   cyc /= cnt;
   double per_iter = cyc / iters;
   double bytes_per_cycle = double(warps) * 32 * X * 4 / per_iter;
-  printf("x%-3d warps %2d mma %d: %.1f cycles/iter/warp, %.0f B/cycle/SM\n", X, warps, mma_on, per_iter, bytes_per_cycle);
+  printf("%s x%-3d warps %2d mma %d: %.1f cycles/iter/warp, %.0f B/cycle/SM\n", SHAPE ? "16x256b" : "32x32b ", X, warps, mma_on, per_iter, bytes_per_cycle);
   cudaFree(out); cudaFree(sink);
 }
 
-int main() {
+int main(int argc, char** argv) {
   int sms = 148;
+  if (argc > 1) {  // 16x256b shape only
+    for (int mma = 0; mma < 2; ++mma)
+      for (int w : {4, 8, 16}) {
+        run<32, 0>(w, mma, sms);
+        run<32, 1>(w, mma, sms);
+        run<64, 1>(w, mma, sms);
+      }
+    return 0;
+  }
   for (int mma = 0; mma < 2; ++mma) {
     for (int w : {4, 8, 16}) {
       run<32>(w, mma, sms);
