@@ -49,7 +49,6 @@ constexpr int kThreads = 32 * (2 + kFoldWarps);  // TMA, MMA, fold
 constexpr int kStageBudget = 160 * 1024;                       // operand ring bytes
 constexpr int kMaxStages = 8;
 constexpr int kXbufBytes = 2 * 16 * 256 * 4;                   // transcripts of 256 hash tiles per slot
-constexpr int kFbufBytes = 2 * kFoldWarps * 64 * 4;            // posted fold values, 2 buffers
 constexpr int kTmemCols = 512;
 constexpr uint16_t kPairMask = 0x3;
 
@@ -78,6 +77,7 @@ struct Smem {
   uint64_t empty[kMaxStages];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
+  uint64_t qbar[4];  // per TMEM lane quadrant: its four fold warps meet here
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -180,8 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_mem = base;
   uint32_t* xbuf = reinterpret_cast<uint32_t*>(base + kStageBudget);
-  uint32_t* fbuf = reinterpret_cast<uint32_t*>(base + kStageBudget + kXbufBytes);
-  Smem& S = *reinterpret_cast<Smem*>(base + kStageBudget + (kReduce ? kXbufBytes + kFbufBytes : 0));
+  Smem& S = *reinterpret_cast<Smem*>(base + kStageBudget + (kReduce ? kXbufBytes : 0));
   volatile int* abort_flag = &S.abort_flag;
 
   const int warp = threadIdx.x / 32;
@@ -205,6 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
       mbar_init(&S.acc_full[i], 1);
       mbar_init(&S.acc_empty[i], 2 * kFoldWarps);  // both CTAs' fold warps release a slot
     }
+    for (int i = 0; i < 4; ++i) mbar_init(&S.qbar[i], 4);
     mbar_init(&S.drain, 1);
     S.abort_flag = 0;
     fence_barrier_init();
@@ -220,6 +220,10 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
   if (warp == 1) {
     tmem_alloc_2sm(&S.tmem_base, kTmemCols);
     tmem_relinquish_2sm();
+  }
+  if (kReduce) {
+    // Transcripts start at zero (the hash step clears them again afterwards).
+    for (int i = threadIdx.x; i < kXbufBytes / 4; i += kThreads) xbuf[i] = 0u;
   }
   tc_fence_before();
   __syncthreads();
@@ -302,11 +306,13 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
         return true;
       };
       auto main_unit = [&](int s, int u) {
+        // Operands first (usually resident already), then the slot.
+        if (!(ok = mbar_wait(&S.full[it % kStages], (it / kStages) & 1, abort_flag, a.sync))) return;
         if ((kReduce || u == 0) && !(ok = acquire(s))) return;
         const uint32_t dt = tmem + 256 * s;
         for (int st = 0; st < stages_per_unit; ++st, ++it) {
           const int j = it % kStages;
-          if (!(ok = mbar_wait(&S.full[j], (it / kStages) & 1, abort_flag, a.sync))) return;
+          if (st > 0 && !(ok = mbar_wait(&S.full[j], (it / kStages) & 1, abort_flag, a.sync))) return;
           tc_fence_after();
           const uint64_t ad = sdesc_kmajor<BK>(sbase + j * kStageBytes);
           const uint64_t bd = sdesc_kmajor<BK>(sbase + j * kStageBytes + kAStage);
@@ -365,16 +371,18 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
     // which reads TMEM about twice as fast as the 16-lane shapes; both
     // 32-column loads of a strip are in flight before the wait.
     //
-    // Fold of one R-chunk: each thread XORs its row's strip values into the
-    // four column classes (col / 2) % 4 of the hash tiles, pairs rows r and
+    // Fold of one R-chunk u: each thread XORs its row's strip values into the
+    // four column classes (col / 2) % 4 of the hash tiles and pairs rows r and
     // r + 8 with one shuffle (lanes with bit 3 clear keep classes 0 and 1,
-    // their partners 2 and 3), and posts the two values to shared memory.
-    // After a barrier of the quadrant's 128 threads, lane p < 16 of warp wi
-    // owns hash tile (row pair p, class wi) = tile q * 64 + wi * 16 + p: it
-    // XORs the four strips' values and rotate-xors the result into word
-    // (chunk % 16) of the tile's transcript in shared memory.  After the last
-    // chunk the owner hashes the transcript.  The quadrant's 16 row pairs are
-    // rows 32 q + (p % 8) + 16 (p / 8) and +8.
+    // their partners 2 and 3).  Word w = u % 16 of a transcript is rotated
+    // by 13 at each later chunk with the same w, so the final transcript is
+    // the XOR over chunks of rotl(fold_u, 13 * (later chunks on w)); the
+    // rotation is linear, so every strip warp pre-rotates its partial fold
+    // and XORs it into the tile's transcript word in shared memory with an
+    // atomic -- no per-chunk combine or barrier.  After the last chunk a
+    // quadrant barrier, then lane p < 16 of warp wi hashes tile (row pair p,
+    // class wi) = q * 64 + wi * 16 + p (rows 32 q + (p % 8) + 16 (p / 8) and
+    // +8) and clears its transcript for the slot's next tile.
     const int fw = warp - 2;
     const int q = warp & 3;
     const int wi = fw >> 2;
@@ -382,22 +390,30 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
     const uint32_t strip_off = (uint32_t(32 * q) << 16) + 64 * wi;
     // Slot releases go to the leader's acc_empty (remotely from the peer).
     const uint32_t rel_base = mapa(&S.acc_empty[0], 0);
-    // Owner lane p reads the posted values of lane src (word cls & 1) of
-    // each strip warp of the quadrant.
+    // Transcript words this lane XORs into: row pair (lane % 8) + 8 (lane / 16),
+    // classes c0 and c0 + 1.
+    const int lane_tile = q * 64 + (is_low ? 0 : 2) * 16 + (lane & 7) + 8 * (lane >> 4);
     const int own_p = lane & 15;
-    const int own_src = (own_p & 7) + 16 * (own_p >> 3) + (wi >= 2 ? 8 : 0);
-    const int own_word = wi & 1;
     const int own_tile = q * 64 + wi * 16 + own_p;
     const int own_row = 32 * q + (own_p & 7) + 16 * (own_p >> 3);
-    uint32_t fpar = 0;    // acc_full parity per slot
-    uint32_t events = 0;  // fold events so far (selects the posting buffer)
+    uint32_t fpar = 0;  // acc_full parity per slot
+    uint32_t qpar = 0;  // qbar parity
     bool ok = true;
+    // The quadrant's four fold warps meet (bounded wait; shared-memory writes
+    // before it are visible after it).
+    auto quadrant_sync = [&]() -> bool {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.qbar[q]);
+      const bool r = mbar_wait(&S.qbar[q], qpar, abort_flag, a.sync);
+      qpar ^= 1u;
+      return r;
+    };
 
     auto fold_slot = [&](auto slot, int u, int tm, int tn) {
       constexpr int s = decltype(slot)::value;
       const bool is_main = u < nmain;
       const bool last_main = u == nmain - 1;
-      if (!(ok = mbar_wait(&S.acc_full[s], bit(fpar, s), abort_flag, a.sync))) return;
+      if (!(ok = mbar_wait_idle(&S.acc_full[s], bit(fpar, s), abort_flag, a.sync))) return;
       fpar ^= 1u << s;
       tc_fence_after();
       const uint32_t taddr = tmem + 256 * s + strip_off;
@@ -410,7 +426,29 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
       tmem_ld32(taddr + 32, v + 32);
       tmem_wait_ld();
       uint32_t p0 = 0, p1 = 0, p2 = 0, p3 = 0;
-      if (do_fold) {
+      if (do_convert) {
+        // S as f32 * 2^-12 for the f16 denoise MMAs (the fold reads the
+        // integer values first).
+        if (do_fold) {
+#pragma unroll
+          for (int i = 0; i < 64; i += 8) {
+            p0 ^= v[i] ^ v[i + 1];
+            p1 ^= v[i + 2] ^ v[i + 3];
+            p2 ^= v[i + 4] ^ v[i + 5];
+            p3 ^= v[i + 6] ^ v[i + 7];
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 64; ++i) v[i] = __float_as_uint(float(int(v[i])) * (1.0f / 4096.0f));
+        tmem_st32(taddr, v);
+        tmem_st32(taddr + 32, v + 32);
+        tmem_wait_st();
+      }
+      // The slot's TMEM traffic is done: release it before any arithmetic.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster_addr(rel_base + 8 * s);
+      if (do_fold && !do_convert) {
 #pragma unroll
         for (int i = 0; i < 64; i += 8) {
           p0 ^= v[i] ^ v[i + 1];
@@ -419,17 +457,6 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
           p3 ^= v[i + 6] ^ v[i + 7];
         }
       }
-      if (do_convert) {
-        // S as f32 * 2^-12 for the f16 denoise MMAs.
-#pragma unroll
-        for (int i = 0; i < 64; ++i) v[i] = __float_as_uint(float(int(v[i])) * (1.0f / 4096.0f));
-        tmem_st32(taddr, v);
-        tmem_st32(taddr + 32, v + 32);
-        tmem_wait_st();
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster_addr(rel_base + 8 * s);
       if (do_store) {
         const int64_t row = int64_t(tm) * BM + int(rank) * BMC + 32 * q + lane;
         const float sa = row < a.M ? a.sA[row] : 0.0f;
@@ -444,46 +471,46 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
       if (do_fold) {
         const uint32_t g0 = __shfl_xor_sync(0xffffffffu, is_low ? p2 : p0, 8);
         const uint32_t g1 = __shfl_xor_sync(0xffffffffu, is_low ? p3 : p1, 8);
-        uint32_t* fb = fbuf + (events & 1) * (kFoldWarps * 64) + q * 256;
-        fb[(wi * 32 + lane) * 2 + 0] = (is_low ? p0 : p2) ^ g0;
-        fb[(wi * 32 + lane) * 2 + 1] = (is_low ? p1 : p3) ^ g1;
-        named_barrier_sync(1 + q, 128);
-        ++events;
-        if (lane < 16) {
-          const uint32_t x = fb[(0 * 32 + own_src) * 2 + own_word] ^ fb[(1 * 32 + own_src) * 2 + own_word] ^
-                             fb[(2 * 32 + own_src) * 2 + own_word] ^ fb[(3 * 32 + own_src) * 2 + own_word];
-          // Transcript words start at zero for every tile: rotl13(0) ^ x = x.
-          uint32_t* tw = xbuf + s * (16 * 256) + (u & 15) * 256 + own_tile;
-          *tw = u < 16 ? x : (rotl13(*tw) ^ x);
-        }
+        const uint32_t f0 = (is_low ? p0 : p2) ^ g0;
+        const uint32_t f1 = (is_low ? p1 : p3) ^ g1;
+        const int w = u & 15;
+        const int later = ((nmain - 1 - w) >> 4) - (u >> 4);  // chunks after u that hit word w
+        const int rot = (13 * later) & 31;
+        uint32_t* tw = xbuf + s * (16 * 256) + w * 256 + lane_tile;
+        atomicXor(tw, __funnelshift_l(f0, f0, rot));
+        atomicXor(tw + 16, __funnelshift_l(f1, f1, rot));
         // The reference counts one hash per 2 x 64 tile of each 128-row
         // tile that starts inside M.
         if (kDebug && lane == 0 && tm * BM + int(rank) * BMC < a.M) atomicAdd(a.counter, 16ull);
-        if (last_main && lane < 16) {
-          // Transcript complete: keyed BLAKE3 and the target compare.
-          const uint32_t* tr = xbuf + s * (16 * 256) + own_tile;
-          uint32_t T[16], key[8], tgt[8], dg[8];
+        if (last_main) {
+          if (!(ok = quadrant_sync())) return;  // every strip's contribution is in
+          if (lane < 16) {
+            // Transcript complete: keyed BLAKE3 and the target compare.
+            uint32_t* tr = xbuf + s * (16 * 256) + own_tile;
+            uint32_t T[16], key[8], dg[8];
 #pragma unroll
-          for (int w = 0; w < 16; ++w) T[w] = w < nmain ? tr[w * 256] : 0u;
+            for (int k = 0; k < 16; ++k) {
+              T[k] = tr[k * 256];
+              tr[k * 256] = 0u;
+            }
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            key[i] = a.key[i];
-            tgt[i] = a.target[i];
+            for (int i = 0; i < 8; ++i) key[i] = a.key[i];
+            b3_compress8(key, T, kB3SingleBlockKeyed, dg);
+            const int tm128 = 2 * tm + int(rank);
+            const int cls = wi;
+            const int64_t grow = int64_t(tm128) * BMC + own_row;
+            const int64_t gcol = int64_t(tn) * BN + 2 * cls;
+            const bool in_bounds = (grow + 8 < a.M) && (gcol + 249 < a.N);
+            if (in_bounds && (a.transcripts || a.digests)) {
+              const int64_t idx = (grow / 16 * 8 + grow % 16) * (a.N / 64) + gcol / 256 * 4 + (gcol % 256) / 2;
+              if (a.transcripts)
+                for (int k = 0; k < 16; ++k) a.transcripts[idx * 16 + k] = T[k];
+              if (a.digests)
+                for (int k = 0; k < 8; ++k) a.digests[idx * 8 + k] = dg[k];
+            }
+            if (in_bounds && u256_le(dg, a.target)) publish_hit(a, tm128, tn, own_row, cls, dg);
           }
-          b3_compress8(key, T, kB3SingleBlockKeyed, dg);
-          const int tm128 = 2 * tm + int(rank);
-          const int cls = wi;
-          const int64_t grow = int64_t(tm128) * BMC + own_row;
-          const int64_t gcol = int64_t(tn) * BN + 2 * cls;
-          const bool in_bounds = (grow + 8 < a.M) && (gcol + 249 < a.N);
-          if (in_bounds && (a.transcripts || a.digests)) {
-            const int64_t idx = (grow / 16 * 8 + grow % 16) * (a.N / 64) + gcol / 256 * 4 + (gcol % 256) / 2;
-            if (a.transcripts)
-              for (int w = 0; w < 16; ++w) a.transcripts[idx * 16 + w] = T[w];
-            if (a.digests)
-              for (int w = 0; w < 8; ++w) a.digests[idx * 8 + w] = dg[w];
-          }
-          if (in_bounds && u256_le(dg, tgt)) publish_hit(a, tm128, tn, own_row, cls, dg);
+          if (!(ok = quadrant_sync())) return;  // cleared before the next tile's first chunk
         }
       }
     };
@@ -518,7 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
 template <int BK, bool R_, bool D_, bool G_>
 int launch_variant(const MainArgs& a, int device, cudaStream_t s) {
   auto kern = noisy_gemm_kernel<BK, R_, D_, G_>;
-  const int smem = kStageBudget + (R_ ? kXbufBytes + kFbufBytes : 0) + int(sizeof(Smem)) + 1024;
+  const int smem = kStageBudget + (R_ ? kXbufBytes : 0) + int(sizeof(Smem)) + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return launch_status();
   cudaLaunchConfig_t cfg = {};

@@ -103,6 +103,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Bounded wait for warps that may idle a long time (no spin on the barrier
+// between polls, so the polling does not compete for issue slots and the
+// shared-memory pipe with latency-critical warps).
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                               SignalSync* sync) {
+  if (mbar_test(bar, parity)) return true;
+  long long t0 = clock64();
+  while (true) {
+    __nanosleep(100);
+    if (mbar_test(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitBudgetCycles) {
+      *abort_flag = 1;
+      record_error(sync, PB2_ERR_DEVICE_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_prefetch(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
