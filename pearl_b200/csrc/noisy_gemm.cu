@@ -45,10 +45,11 @@ constexpr int BM = 2 * BMC;  // rows per pair tile
 constexpr int BN = 256;
 constexpr int kTileK = 128;  // the reference's tile_size_k (K must be a multiple)
 constexpr int kFoldWarps = 16;
-constexpr int kThreads = 32 * (2 + kFoldWarps);  // TMA, MMA, fold
+constexpr int kHashWarps = 2;
+constexpr int kThreads = 32 * (2 + kFoldWarps + kHashWarps);  // TMA, MMA, fold, hash
 constexpr int kStageBudget = 160 * 1024;                       // operand ring bytes
 constexpr int kMaxStages = 8;
-constexpr int kXbufBytes = 2 * 16 * 256 * 4;                   // transcripts of 256 hash tiles per slot
+constexpr int kXbufBytes = 4 * 16 * 256 * 4;  // transcripts of 256 hash tiles, 2 slots x 2 tiles in flight
 constexpr int kTmemCols = 512;
 constexpr uint16_t kPairMask = 0x3;
 
@@ -77,7 +78,8 @@ struct Smem {
   uint64_t empty[kMaxStages];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
-  uint64_t qbar[4];  // per TMEM lane quadrant: its four fold warps meet here
+  uint64_t xready[4];  // transcript buffer 2 * slot + (round & 1) is complete
+  uint64_t xfree[4];   // ... has been hashed and cleared
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -204,7 +206,10 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
       mbar_init(&S.acc_full[i], 1);
       mbar_init(&S.acc_empty[i], 2 * kFoldWarps);  // both CTAs' fold warps release a slot
     }
-    for (int i = 0; i < 4; ++i) mbar_init(&S.qbar[i], 4);
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&S.xready[i], kFoldWarps);
+      mbar_init(&S.xfree[i], kHashWarps);
+    }
     mbar_init(&S.drain, 1);
     S.abort_flag = 0;
     fence_barrier_init();
@@ -363,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
       while (!mbar_test(&S.drain, 0) && clock64() - t0 < 100000000LL) {
       }
     }
-  } else {
+  } else if (warp < 2 + kFoldWarps) {
     // ------------------------------------------------------------ fold warps
     // Four warps per TMEM lane quadrant q = warp % 4 (the quadrant a warp may
     // access); warp index wi = 0..3 within the quadrant picks the 64-column
@@ -379,10 +384,10 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
     // the XOR over chunks of rotl(fold_u, 13 * (later chunks on w)); the
     // rotation is linear, so every strip warp pre-rotates its partial fold
     // and XORs it into the tile's transcript word in shared memory with an
-    // atomic -- no per-chunk combine or barrier.  After the last chunk a
-    // quadrant barrier, then lane p < 16 of warp wi hashes tile (row pair p,
-    // class wi) = q * 64 + wi * 16 + p (rows 32 q + (p % 8) + 16 (p / 8) and
-    // +8) and clears its transcript for the slot's next tile.
+    // atomic -- no per-chunk combine or barrier.  Each slot has two
+    // transcript buffers (alternating rounds); after a tile's last chunk the
+    // hash warps take the buffer over while the slot's next tile fills the
+    // other one.
     const int fw = warp - 2;
     const int q = warp & 3;
     const int wi = fw >> 2;
@@ -393,24 +398,12 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
     // Transcript words this lane XORs into: row pair (lane % 8) + 8 (lane / 16),
     // classes c0 and c0 + 1.
     const int lane_tile = q * 64 + (is_low ? 0 : 2) * 16 + (lane & 7) + 8 * (lane >> 4);
-    const int own_p = lane & 15;
-    const int own_tile = q * 64 + wi * 16 + own_p;
-    const int own_row = 32 * q + (own_p & 7) + 16 * (own_p >> 3);
     uint32_t fpar = 0;  // acc_full parity per slot
-    uint32_t qpar = 0;  // qbar parity
     bool ok = true;
-    // The quadrant's four fold warps meet (bounded wait; shared-memory writes
-    // before it are visible after it).
-    auto quadrant_sync = [&]() -> bool {
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&S.qbar[q]);
-      const bool r = mbar_wait(&S.qbar[q], qpar, abort_flag, a.sync);
-      qpar ^= 1u;
-      return r;
-    };
 
-    auto fold_slot = [&](auto slot, int u, int tm, int tn) {
+    auto fold_slot = [&](auto slot, int round, int u, int tm, int tn) {
       constexpr int s = decltype(slot)::value;
+      const int b = 2 * s + (round & 1);  // transcript buffer
       const bool is_main = u < nmain;
       const bool last_main = u == nmain - 1;
       if (!(ok = mbar_wait_idle(&S.acc_full[s], bit(fpar, s), abort_flag, a.sync))) return;
@@ -476,41 +469,20 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
         const int w = u & 15;
         const int later = ((nmain - 1 - w) >> 4) - (u >> 4);  // chunks after u that hit word w
         const int rot = (13 * later) & 31;
-        uint32_t* tw = xbuf + s * (16 * 256) + w * 256 + lane_tile;
+        // A tile's first chunk reuses the buffer of two rounds ago: the hash
+        // warps must have cleared it.
+        if (u == 0 && round >= 2 &&
+            !(ok = mbar_wait_idle(&S.xfree[b], ((round >> 1) - 1) & 1, abort_flag, a.sync)))
+          return;
+        uint32_t* tw = xbuf + b * (16 * 256) + w * 256 + lane_tile;
         atomicXor(tw, __funnelshift_l(f0, f0, rot));
         atomicXor(tw + 16, __funnelshift_l(f1, f1, rot));
         // The reference counts one hash per 2 x 64 tile of each 128-row
         // tile that starts inside M.
         if (kDebug && lane == 0 && tm * BM + int(rank) * BMC < a.M) atomicAdd(a.counter, 16ull);
         if (last_main) {
-          if (!(ok = quadrant_sync())) return;  // every strip's contribution is in
-          if (lane < 16) {
-            // Transcript complete: keyed BLAKE3 and the target compare.
-            uint32_t* tr = xbuf + s * (16 * 256) + own_tile;
-            uint32_t T[16], key[8], dg[8];
-#pragma unroll
-            for (int k = 0; k < 16; ++k) {
-              T[k] = tr[k * 256];
-              tr[k * 256] = 0u;
-            }
-#pragma unroll
-            for (int i = 0; i < 8; ++i) key[i] = a.key[i];
-            b3_compress8(key, T, kB3SingleBlockKeyed, dg);
-            const int tm128 = 2 * tm + int(rank);
-            const int cls = wi;
-            const int64_t grow = int64_t(tm128) * BMC + own_row;
-            const int64_t gcol = int64_t(tn) * BN + 2 * cls;
-            const bool in_bounds = (grow + 8 < a.M) && (gcol + 249 < a.N);
-            if (in_bounds && (a.transcripts || a.digests)) {
-              const int64_t idx = (grow / 16 * 8 + grow % 16) * (a.N / 64) + gcol / 256 * 4 + (gcol % 256) / 2;
-              if (a.transcripts)
-                for (int k = 0; k < 16; ++k) a.transcripts[idx * 16 + k] = T[k];
-              if (a.digests)
-                for (int k = 0; k < 8; ++k) a.digests[idx * 8 + k] = dg[k];
-            }
-            if (in_bounds && u256_le(dg, a.target)) publish_hit(a, tm128, tn, own_row, cls, dg);
-          }
-          if (!(ok = quadrant_sync())) return;  // cleared before the next tile's first chunk
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&S.xready[b]);  // this warp's contributions are in
         }
       }
     };
@@ -520,13 +492,65 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
       int tm0, tn0, tm1 = 0, tn1 = 0;
       tile_coords(a, t0, tm0, tn0);
       if (two) tile_coords(a, t0 + 1, tm1, tn1);
+      const int round = (t0 - first) / stride;
       for (int u = 0; u < units && ok; ++u) {
         const bool is_main = u < nmain;
         const bool event = (is_main && (kReduce || u == nmain - 1)) || (!is_main && u == units - 1);
         if (!event) continue;
-        fold_slot(I0{}, u, tm0, tn0);
-        if (two && ok) fold_slot(I1{}, u, tm1, tn1);
+        fold_slot(I0{}, round, u, tm0, tn0);
+        if (two && ok) fold_slot(I1{}, round, u, tm1, tn1);
       }
+    }
+  } else if (kReduce) {
+    // ------------------------------------------------------------ hash warps
+    // Thread j hashes tiles j + 64 i (i < 4) of a finished transcript buffer;
+    // tile q * 64 + c * 16 + p is row pair p (rows 32 q + (p % 8) + 16 (p / 8)
+    // and +8) of lane quadrant q, column class c.  Each word is cleared after
+    // it is read, for the slot's tile two rounds later.
+    const int j = (warp - 2 - kFoldWarps) * 32 + lane;
+    bool ok = true;
+    auto hash_buffer = [&](auto slot, int round, int tm, int tn) {
+      const int b = 2 * decltype(slot)::value + (round & 1);
+      if (!(ok = mbar_wait_idle(&S.xready[b], (round >> 1) & 1, abort_flag, a.sync))) return;
+      const int tm128 = 2 * tm + int(rank);
+#pragma unroll 1
+      for (int i = 0; i < 4; ++i) {
+        const int ht = j + 64 * i;
+        uint32_t* tr = xbuf + b * (16 * 256) + ht;
+        uint32_t T[16], key[8], dg[8];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          T[k] = tr[k * 256];
+          tr[k * 256] = 0u;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) key[k] = a.key[k];
+        b3_compress8(key, T, kB3SingleBlockKeyed, dg);
+        const int hq = ht >> 6, cls = (ht >> 4) & 3, p = ht & 15;
+        const int row_in_tile = 32 * hq + (p & 7) + 16 * (p >> 3);
+        const int64_t grow = int64_t(tm128) * BMC + row_in_tile;
+        const int64_t gcol = int64_t(tn) * BN + 2 * cls;
+        const bool in_bounds = (grow + 8 < a.M) && (gcol + 249 < a.N);
+        if (in_bounds && (a.transcripts || a.digests)) {
+          const int64_t idx = (grow / 16 * 8 + grow % 16) * (a.N / 64) + gcol / 256 * 4 + (gcol % 256) / 2;
+          if (a.transcripts)
+            for (int k = 0; k < 16; ++k) a.transcripts[idx * 16 + k] = T[k];
+          if (a.digests)
+            for (int k = 0; k < 8; ++k) a.digests[idx * 8 + k] = dg[k];
+        }
+        if (in_bounds && u256_le(dg, a.target)) publish_hit(a, tm128, tn, row_in_tile, cls, dg);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.xfree[b]);
+    };
+    for (int t0 = first; t0 < a.num_tiles && ok; t0 += stride) {
+      const bool two = t0 + 1 < a.num_tiles;
+      const int round = (t0 - first) / stride;
+      int tm0, tn0, tm1 = 0, tn1 = 0;
+      tile_coords(a, t0, tm0, tn0);
+      if (two) tile_coords(a, t0 + 1, tm1, tn1);
+      hash_buffer(I0{}, round, tm0, tn0);
+      if (two && ok) hash_buffer(I1{}, round, tm1, tn1);
     }
   }
 
