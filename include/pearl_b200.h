@@ -39,6 +39,7 @@ extern "C" {
 #define PB2_ERR_CUDA 3               /* a CUDA runtime call failed */
 #define PB2_ERR_DEVICE_TIMEOUT 4     /* a bounded device-side wait ran out */
 #define PB2_ERR_NO_DRIVER_ENTRY 5    /* cuTensorMapEncodeTiled unavailable */
+#define PB2_ERR_SCRATCH_LIMIT 6      /* problem exceeds PB2_STATIC_SCRATCH_BYTES */
 
 /* Sizes of the caller-owned signalling buffers.
  * Header: byte-compatible with the reference HostSignalHeader
@@ -196,6 +197,30 @@ PB2_API int pb2_noisy_gemm(const pb2_gemm_params* p, void* stream);
 /* Plain scaled GEMM: C = bf16(A_scales * (A . B^T) * B_scales), reading the
  * operands from p->ApEA / p->BpEB (the reference passes A and B there). */
 PB2_API int pb2_gemm(const pb2_gemm_params* p, void* stream);
+
+/* ------------------------------------------- noisy_gemm, static scratch ---
+ * No counterpart in the reference.  The same mined GEMM as pb2_noisy_gemm,
+ * for callers that cannot allocate device memory: a host that only reaches
+ * this library through its C ABI and has no device allocator, or a process
+ * whose HBM is owned by another allocator (an inference server's memory pool
+ * takes most of it at start-up, so a cudaMalloc can fail, and a cudaFree
+ * stalls the whole device).  The exact int32 noising projections, which
+ * pb2_noisy_gemm reads from the caller's AxEBL_int32 / EARxBpEB_int32, live
+ * in a fixed array inside the library instead; p->AxEBL_int32 and
+ * p->EARxBpEB_int32 must be NULL.  Every other argument, and every result,
+ * is as for pb2_noisy_gemm (the caller still passes all inputs and outputs).
+ *   Limit: (m if run_noising_a) * r + (n if run_noising_b) * r int32 words
+ *   must fit in PB2_STATIC_SCRATCH_BYTES (8 MiB: m + n <= 16384 at r = 128);
+ *   larger problems return PB2_ERR_SCRATCH_LIMIT before any work is queued.
+ * Each GPU that loads the library holds the array until the process exits.
+ * The first call on a device looks up the array's device address (with that
+ * device current) and caches it; make that first call before any stream
+ * capture.  No call allocates device or host memory.  All calls on a device
+ * share the array, which keeps the last call's contents: each call clears
+ * the words it uses on `stream` first, and calls that overlap on the GPU
+ * (unordered streams) race on it. */
+#define PB2_STATIC_SCRATCH_BYTES (8 * 1024 * 1024)
+PB2_API int pb2_noisy_gemm_static_scratch(const pb2_gemm_params* p, void* stream);
 
 /* -------------------------------------------------------------- inner_hash -
  * Replaces inner_hash (pearl_gemm_api.cpp:939-970, inner_hash_kernel.cu:11-58):

@@ -20,6 +20,8 @@ PB2_ERR_UNSUPPORTED_CONFIG = 2
 PB2_ERR_CUDA = 3
 PB2_ERR_DEVICE_TIMEOUT = 4
 PB2_ERR_NO_DRIVER_ENTRY = 5
+PB2_ERR_SCRATCH_LIMIT = 6
+STATIC_SCRATCH_BYTES = 8 * 1024 * 1024
 
 HOST_SIGNAL_HEADER_SIZE = 640
 HOST_SIGNAL_SYNC_SIZE = 16
@@ -29,6 +31,7 @@ EXPORTED = [
     "pb2_host_signal_header_size", "pb2_host_signal_sync_size", "pb2_status_string",
     "pb2_last_cuda_error", "pb2_abi_version", "pb2_noise_gen", "pb2_noise_A", "pb2_noise_B",
     "pb2_denoise_converter", "pb2_noisy_gemm", "pb2_gemm", "pb2_inner_hash",
+    "pb2_noisy_gemm_static_scratch",
 ]
 
 _vp = ctypes.c_void_p
@@ -93,7 +96,7 @@ def load() -> ctypes.CDLL:
                 "`python -m pearl_b200.build` (there is no CPU fallback)")
         L = ctypes.CDLL(LIB_PATH)
         for name in ("pb2_noise_gen", "pb2_noise_A", "pb2_noise_B", "pb2_denoise_converter",
-                     "pb2_noisy_gemm", "pb2_gemm"):
+                     "pb2_noisy_gemm", "pb2_gemm", "pb2_noisy_gemm_static_scratch"):
             getattr(L, name).restype = ctypes.c_int
             getattr(L, name).argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         L.pb2_inner_hash.restype = ctypes.c_int

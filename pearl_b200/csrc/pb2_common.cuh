@@ -492,4 +492,7 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
 int set_device(int device);
 int sm_count(int device);
 int launch_status();
+// PB2_OK for cudaSuccess, else PB2_ERR_CUDA with the error's text recorded
+// for pb2_last_cuda_error.
+int cuda_status(cudaError_t e);
 }  // namespace pb2

@@ -76,6 +76,8 @@ int sm_count(int device) {
 
 int launch_status() { return note_cuda(cudaGetLastError()); }
 
+int cuda_status(cudaError_t e) { return note_cuda(e); }
+
 }  // namespace pb2
 
 extern "C" {
@@ -98,6 +100,8 @@ const char* pb2_status_string(int status) {
       return "a device-side wait ran out of its budget";
     case PB2_ERR_NO_DRIVER_ENTRY:
       return "cuTensorMapEncodeTiled is not available from the driver";
+    case PB2_ERR_SCRATCH_LIMIT:
+      return "problem too large for the library's static scratch (PB2_STATIC_SCRATCH_BYTES)";
     default:
       return "unknown status";
   }
