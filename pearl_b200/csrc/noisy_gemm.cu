@@ -47,9 +47,13 @@ constexpr int kTileK = 128;  // the reference's tile_size_k (K must be a multipl
 constexpr int kFoldWarps = 16;
 constexpr int kHashWarps = 2;
 constexpr int kThreads = 32 * (2 + kFoldWarps + kHashWarps);  // TMA, MMA, fold, hash
-constexpr int kStageBudget = 160 * 1024;                       // operand ring bytes
+// Operand ring bytes: shared memory (227 KB per CTA) also holds the C boxes
+// and, with the transcript, 64 KB of transcript buffers.
+constexpr int stage_budget(bool reduce) { return reduce ? 128 * 1024 : 160 * 1024; }
 constexpr int kMaxStages = 8;
 constexpr int kXbufBytes = 4 * 16 * 256 * 4;  // transcripts of 256 hash tiles, 2 slots x 2 tiles in flight
+constexpr int kCBoxBytes = 32 * 32 * 2;         // one fold warp's C box: 32 rows x 32 bf16 columns
+constexpr int kCStageBytes = kFoldWarps * kCBoxBytes;
 constexpr int kTmemCols = 512;
 constexpr uint16_t kPairMask = 0x3;
 
@@ -57,6 +61,7 @@ struct MainArgs {
   CUtensorMap tmA, tmB;      // ApEA (m,k), BpEB (n,k): int8, boxes of 128 rows
   CUtensorMap tmDA0, tmDB0;  // EAL_fp16 (m,r), EARxBpEB_fp16 (n,r)
   CUtensorMap tmDA1, tmDB1;  // AxEBL_fp16 (m,r), EBR_fp16 (n,r)
+  CUtensorMap tmC;           // C (m,n) bf16, 32 x 32 boxes, 64-byte swizzle
   int M, N, K, R;
   int tiles_m, tiles_n, num_tiles, group;
   const float* sA;
@@ -75,8 +80,8 @@ struct MainArgs {
 
 struct Smem {
   uint64_t full[kMaxStages];
-  uint64_t empty[kMaxStages];
-  uint64_t acc_full[2];
+  uint64_t empty[kMaxStages];  // stage consumed: also "this transcript chunk is final"
+  uint64_t acc_full[2];        // the slot's accumulator is final (denoise / store events)
   uint64_t acc_empty[2];
   uint64_t xready[4];  // transcript buffer 2 * slot + (round & 1) is complete
   uint64_t xfree[4];   // ... has been hashed and cleared
@@ -103,27 +108,49 @@ __device__ __forceinline__ uint32_t pack_bf16(float x, float y) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Scale 32 consecutive accumulator columns of one row and store them as bf16.
+// One fold warp's 32 x 32 block of C (lane = row, v = 32 consecutive
+// accumulator columns of the lane's row): scale, convert to bf16, write the
+// block into the warp's shared-memory box and hand it to a TMA store, which
+// writes whole lines and clips rows >= M and columns >= N.  Writing C straight
+// from registers would scatter every store instruction over 32 rows, and the
+// fold warps would spend thousands of cycles in the store unit while the MMA
+// issuer waits for their next release.
 template <bool kFloatAcc>
-__device__ __forceinline__ void store_c32(const MainArgs& a, const uint32_t* v, int64_t row,
-                                          int col0, float row_scale) {
-  if (row >= a.M) return;
+__device__ __forceinline__ void store_c_block(const MainArgs& a, uint8_t* box, const uint32_t* v,
+                                              int row0, int col0, float row_scale, int lane) {
+  if (lane == 0) bulk_wait_read_all();  // the box's previous store has read it
+  __syncwarp();
   const float4* sb = reinterpret_cast<const float4*>(a.sB + col0);
+  uint32_t w[16];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const int c = col0 + 8 * j;
-    if (c + 8 > a.N) break;
-    float4 b0 = sb[2 * j], b1 = sb[2 * j + 1];
+    float4 b0 = make_float4(0.f, 0.f, 0.f, 0.f), b1 = b0;
+    if (col0 + 8 * j < a.N) {  // N % 8 == 0: a group of 8 columns is all in or all out
+      b0 = sb[2 * j];
+      b1 = sb[2 * j + 1];
+    }
     float f[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
       f[i] = kFloatAcc ? __uint_as_float(v[8 * j + i]) : float(int(v[8 * j + i]));
-    uint4 o;
-    o.x = pack_bf16(f[0] * row_scale * b0.x, f[1] * row_scale * b0.y);
-    o.y = pack_bf16(f[2] * row_scale * b0.z, f[3] * row_scale * b0.w);
-    o.z = pack_bf16(f[4] * row_scale * b1.x, f[5] * row_scale * b1.y);
-    o.w = pack_bf16(f[6] * row_scale * b1.z, f[7] * row_scale * b1.w);
-    *reinterpret_cast<uint4*>(a.C + row * int64_t(a.N) + c) = o;
+    w[4 * j + 0] = pack_bf16(f[0] * row_scale * b0.x, f[1] * row_scale * b0.y);
+    w[4 * j + 1] = pack_bf16(f[2] * row_scale * b0.z, f[3] * row_scale * b0.w);
+    w[4 * j + 2] = pack_bf16(f[4] * row_scale * b1.x, f[5] * row_scale * b1.y);
+    w[4 * j + 3] = pack_bf16(f[6] * row_scale * b1.z, f[7] * row_scale * b1.w);
+  }
+  // 64-byte swizzle (the tensor map's): 16-byte chunk k of row r sits at
+  // chunk k ^ ((r >> 1) & 3), which also spreads a store instruction's 32
+  // lanes over all banks.
+  uint8_t* rowp = box + lane * 64;
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    *reinterpret_cast<uint4*>(rowp + ((k ^ ((lane >> 1) & 3)) << 4)) =
+        make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(&a.tmC, box, col0, row0);
+    bulk_commit_group();
   }
 }
 
@@ -173,8 +200,11 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
   constexpr int kAStage = BMC * BK;        // this CTA's 128 rows of A
   constexpr int kBStage = (BN / 2) * BK;   // this CTA's half of the 256 rows of B
   constexpr int kStageBytes = kAStage + kBStage;
+  constexpr int kStageBudget = stage_budget(kReduce);
   constexpr int kStages =
       (kStageBudget / kStageBytes) < kMaxStages ? (kStageBudget / kStageBytes) : kMaxStages;
+  static_assert(kStageBudget + (kReduce ? kXbufBytes : 0) + kCStageBytes + 1024 + 256 <= 232448,
+                "shared memory plan exceeds 227 KB");
   constexpr uint32_t kIdescI8 = idesc_i8(BM, BN);
   constexpr uint32_t kIdescF16 = idesc_f16(BM, BN);
 
@@ -182,7 +212,8 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_mem = base;
   uint32_t* xbuf = reinterpret_cast<uint32_t*>(base + kStageBudget);
-  Smem& S = *reinterpret_cast<Smem*>(base + kStageBudget + (kReduce ? kXbufBytes : 0));
+  uint8_t* cstage = base + kStageBudget + (kReduce ? kXbufBytes : 0);
+  Smem& S = *reinterpret_cast<Smem*>(cstage + kCStageBytes);
   volatile int* abort_flag = &S.abort_flag;
 
   const int warp = threadIdx.x / 32;
@@ -217,6 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
   if (warp == 0 && lane == 0) {
     tma_prefetch(&a.tmA);
     tma_prefetch(&a.tmB);
+    tma_prefetch(&a.tmC);
     if (kDenoise) {
       tma_prefetch(&a.tmDA0); tma_prefetch(&a.tmDB0);
       tma_prefetch(&a.tmDA1); tma_prefetch(&a.tmDB1);
@@ -299,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
     if (lane == 0 && rank == 0) {
       uint32_t it = 0;
       uint32_t empar = 0;  // acc_empty parity per slot
-      uint32_t pend = 0;   // bit s: an acc_full commit of slot s awaits the fold warps' release
+      uint32_t pend = 0;   // bit s: slot s holds a unit the fold warps have not released yet
       bool ok = true;
       const uint32_t sbase = smem_u32(stage_mem);
       auto acquire = [&](int s) -> bool {
@@ -326,10 +358,11 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
           for (int ks = 1; ks < BK / 32; ++ks) umma_i8_2sm(dt, ad + 2 * ks, bd + 2 * ks, kIdescI8, 1);
           umma_commit_2sm(&S.empty[j], kPairMask);
         }
-        if (kReduce || u == nmain - 1) {
-          umma_commit_2sm(&S.acc_full[s], kPairMask);
-          pend |= 1u << s;
-        }
+        // With the transcript every unit is a fold event, and the stage's
+        // commit above doubles as "accumulator ready" (one commit per unit
+        // keeps the tensor pipe's queue full).  A lone event gets its own.
+        if (!kReduce && u == nmain - 1) umma_commit_2sm(&S.acc_full[s], kPairMask);
+        if (kReduce || u == nmain - 1) pend |= 1u << s;
       };
       auto denoise_unit = [&](int s, int d) {
         if (d == 0 && !(ok = acquire(s))) return;  // S has been rewritten as f32
@@ -401,13 +434,28 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
     uint32_t fpar = 0;  // acc_full parity per slot
     bool ok = true;
 
-    auto fold_slot = [&](auto slot, int round, int u, int tm, int tn) {
+    // Transcript chunks (every main unit when kReduce) are final when the
+    // commit that frees the unit's last operand stage fires: empty[] of that
+    // stage, phase = stage count / kStages.  A parity wait is exact only if
+    // the barrier has completed the phase before it -- true here, because
+    // these warps waited for the slot's previous unit, which came later in
+    // the issue order than the stage's previous use -- and if the phase
+    // cannot be overtaken, which it cannot: the issuer reuses the slot, and
+    // so comes within kStages units of refilling the stage, only after these
+    // warps release it.  Lone events (the f32 rewrite without a transcript,
+    // the final store) have no such neighbour and wait on acc_full instead.
+    auto fold_slot = [&](auto slot, int round, int u, int tm, int tn, uint32_t last_stage) {
       constexpr int s = decltype(slot)::value;
       const int b = 2 * s + (round & 1);  // transcript buffer
       const bool is_main = u < nmain;
       const bool last_main = u == nmain - 1;
-      if (!(ok = mbar_wait_idle(&S.acc_full[s], bit(fpar, s), abort_flag, a.sync))) return;
-      fpar ^= 1u << s;
+      if (kReduce && is_main) {
+        if (!(ok = mbar_wait(&S.empty[last_stage % kStages], (last_stage / kStages) & 1, abort_flag, a.sync)))
+          return;
+      } else {
+        if (!(ok = mbar_wait(&S.acc_full[s], bit(fpar, s), abort_flag, a.sync))) return;
+        fpar ^= 1u << s;
+      }
       tc_fence_after();
       const uint32_t taddr = tmem + 256 * s + strip_off;
       const bool do_fold = kReduce && is_main;
@@ -438,9 +486,18 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
         tmem_wait_st();
       }
       // The slot's TMEM traffic is done: release it before any arithmetic.
+      // After loads only (drained by wait::ld) a relaxed arrive suffices, and
+      // it never waits for this warp's C stores still in flight; after the
+      // f32 rewrite the arrive must release the tcgen05.st to the issuer's
+      // MMAs (cluster scope: the peer's stores feed the leader's MMAs).
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster_addr(rel_base + 8 * s);
+      if (lane == 0) {
+        if (do_convert)
+          mbar_arrive_remote(rel_base + 8 * s);
+        else
+          mbar_arrive_relaxed_cluster(rel_base + 8 * s);
+      }
       if (do_fold && !do_convert) {
 #pragma unroll
         for (int i = 0; i < 64; i += 8) {
@@ -448,17 +505,6 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
           p1 ^= v[i + 2] ^ v[i + 3];
           p2 ^= v[i + 4] ^ v[i + 5];
           p3 ^= v[i + 6] ^ v[i + 7];
-        }
-      }
-      if (do_store) {
-        const int64_t row = int64_t(tm) * BM + int(rank) * BMC + 32 * q + lane;
-        const float sa = row < a.M ? a.sA[row] : 0.0f;
-        if (!is_main) {
-          store_c32<true>(a, v, row, tn * BN + 64 * wi, sa * 4096.0f);
-          store_c32<true>(a, v + 32, row, tn * BN + 64 * wi + 32, sa * 4096.0f);
-        } else {
-          store_c32<false>(a, v, row, tn * BN + 64 * wi, sa);
-          store_c32<false>(a, v + 32, row, tn * BN + 64 * wi + 32, sa);
         }
       }
       if (do_fold) {
@@ -485,8 +531,24 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
           if (lane == 0) mbar_arrive(&S.xready[b]);  // this warp's contributions are in
         }
       }
+      // C last: the transcript is complete and the hash warps can start.
+      if (do_store) {
+        const int row0 = tm * BM + int(rank) * BMC + 32 * q;
+        const int row = row0 + lane;
+        const float sa = row < a.M ? a.sA[row] : 0.0f;
+        uint8_t* box = cstage + fw * kCBoxBytes;
+        const int col = tn * BN + 64 * wi;
+        if (!is_main) {
+          store_c_block<true>(a, box, v, row0, col, sa * 4096.0f, lane);
+          store_c_block<true>(a, box, v + 32, row0, col + 32, sa * 4096.0f, lane);
+        } else {
+          store_c_block<false>(a, box, v, row0, col, sa, lane);
+          store_c_block<false>(a, box, v + 32, row0, col + 32, sa, lane);
+        }
+      }
     };
 
+    uint32_t it = 0;  // operand stages issued so far, in the issuer's order
     for (int t0 = first; t0 < a.num_tiles && ok; t0 += stride) {
       const bool two = t0 + 1 < a.num_tiles;
       int tm0, tn0, tm1 = 0, tn1 = 0;
@@ -496,11 +558,14 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
       for (int u = 0; u < units && ok; ++u) {
         const bool is_main = u < nmain;
         const bool event = (is_main && (kReduce || u == nmain - 1)) || (!is_main && u == units - 1);
+        const uint32_t it0 = it;
+        it += uint32_t((two ? 2 : 1) * stages_per_unit);
         if (!event) continue;
-        fold_slot(I0{}, round, u, tm0, tn0);
-        if (two && ok) fold_slot(I1{}, round, u, tm1, tn1);
+        fold_slot(I0{}, round, u, tm0, tn0, it0 + stages_per_unit - 1);
+        if (two && ok) fold_slot(I1{}, round, u, tm1, tn1, it0 + 2 * stages_per_unit - 1);
       }
     }
+    if (lane == 0) bulk_wait_all();  // C is written before the kernel ends
   } else if (kReduce) {
     // ------------------------------------------------------------ hash warps
     // Thread j hashes tiles j + 64 i (i < 4) of a finished transcript buffer;
@@ -569,7 +634,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
 template <int BK, bool R_, bool D_, bool G_>
 int launch_variant(const MainArgs& a, int device, cudaStream_t s) {
   auto kern = noisy_gemm_kernel<BK, R_, D_, G_>;
-  const int smem = kStageBudget + (R_ ? kXbufBytes : 0) + int(sizeof(Smem)) + 1024;
+  const int smem = stage_budget(R_) + (R_ ? kXbufBytes : 0) + kCStageBytes + int(sizeof(Smem)) + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return launch_status();
   cudaLaunchConfig_t cfg = {};
@@ -645,6 +710,9 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
   if ((st = make_tmap_2d(&a.tmA, p.ApEA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.k, p.m, bk, BMC, swz)))
     return st;
   if ((st = make_tmap_2d(&a.tmB, p.BpEB, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.k, p.n, bk, BN / 2, swz)))
+    return st;
+  if ((st = make_tmap_2d(&a.tmC, p.C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.n, p.m, 32, 32,
+                         CU_TENSOR_MAP_SWIZZLE_64B)))
     return st;
   if (denoise) {
     const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;

@@ -136,6 +136,26 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
+// 2-D tiled store of a shared-memory box to global memory (bulk async group
+// of the calling thread; elements outside the tensor are not written).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until this thread's bulk stores have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Wait until this thread's bulk stores are complete (written to global).
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // Named barrier among `count` threads (a multiple of 32) of the CTA.
 __device__ __forceinline__ void named_barrier_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
@@ -167,6 +187,12 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t remote_bar) {
 // follow completed tcgen05.ld / shared-memory traffic of this thread.
 __device__ __forceinline__ void mbar_arrive_cluster_addr(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+// Arrive with relaxed semantics: orders nothing, so it never waits for this
+// thread's outstanding global stores.  For releases whose only hazard is
+// tensor memory that tcgen05.wait::ld has already drained.
+__device__ __forceinline__ void mbar_arrive_relaxed_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 __device__ __forceinline__ int4 ld_cluster_v4(uint32_t addr) {
   int4 v;
