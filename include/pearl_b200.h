@@ -63,6 +63,53 @@ PB2_API const char* pb2_last_cuda_error(void);
 /* ABI version of the loaded library (PB2_ABI_VERSION). */
 PB2_API int pb2_abi_version(void);
 
+/* ----------------------------------------------------------- tensor_hash ---
+ * Replaces tensor_hash (tensor_hash_api.hpp:45-120; kernels
+ * merkle_tree_roots_kernel.hpp, compute_blake_mt_kernel.hpp,
+ * reduce_roots_kernel.h): out = BLAKE3 keyed by `key` of the `len` bytes at
+ * `data` zero-padded to whole 1 KiB chunks.  `roots` is caller scratch of at
+ * least pb2_required_scratchpad_bytes(len, threads_per_block) bytes (one
+ * 32-byte subtree root per group of threads_per_block chunks).  data must be
+ * 16-byte aligned; key, out and roots 4-byte aligned; all on `device`.
+ * threads_per_block in {128, 256, 512}; the reference's num_stages and
+ * leaves_per_mt_block tuning knobs have no counterpart here. */
+typedef struct pb2_tensor_hash_params {
+  int device;
+  const uint8_t* data;
+  int64_t len;
+  const uint8_t* key; /* 32 bytes */
+  uint8_t* out;       /* 32 bytes */
+  uint8_t* roots;     /* scratch */
+  int64_t roots_bytes;
+  int threads_per_block;
+} pb2_tensor_hash_params;
+PB2_API int pb2_tensor_hash(const pb2_tensor_hash_params* p, void* stream);
+/* Replaces get_required_scratchpad_bytes (tensor_hash_api.hpp:37-43). */
+PB2_API int64_t pb2_required_scratchpad_bytes(int64_t matrix_bytes, int threads_per_block);
+
+/* ------------------------------------- commitment_hash_from_merkle_roots ---
+ * Replaces commitment_hash_from_merkle_roots (tensor_hash_api.hpp:124-212,
+ * commitment_hash_from_merkle_roots_kernel.hpp): the noise seeds
+ *   B_commitment_hash = BLAKE3(key || B_root'),
+ *   A_commitment_hash = BLAKE3(B_commitment_hash || A_root'),
+ * where with `salted` each root is first bound to its matrix dimension
+ * (V3 seeds) and, when routing_root / offsets_hash are given (MoE),
+ * A_root' = BLAKE3(A_root || BLAKE3(routing_root || offsets_hash)).
+ * All buffers are 32 bytes on `device`, 4-byte aligned. */
+typedef struct pb2_commitment_params {
+  int device;
+  const uint8_t* A_merkle_root;
+  const uint8_t* B_merkle_root;
+  const uint8_t* key;
+  uint8_t* A_commitment_hash;
+  uint8_t* B_commitment_hash;
+  const uint8_t* routing_root; /* optional, with offsets_hash */
+  const uint8_t* offsets_hash;
+  int salted;
+  uint32_t salted_dim_a, salted_dim_b;
+} pb2_commitment_params;
+PB2_API int pb2_commitment_hash_from_merkle_roots(const pb2_commitment_params* p, void* stream);
+
 /* ------------------------------------------------------------- noise_gen ---
  * Replaces noise_gen (pearl_gemm_api.cpp:168-298; kernel
  * noise_generation_kernel.h:88-758).  Any output may be NULL (not produced).

@@ -4,7 +4,8 @@ the ``pearl_gemm`` package surface (miner/pearl-gemm/src/pearl_gemm/__init__.py)
     import pearl_b200 as pearl_gemm
 
 gives the reference's operators (noise_gen, noise_A, noise_B, gemm,
-noisy_gemm, denoise_converter), helpers and constants, and registers the same
+noisy_gemm, denoise_converter, tensor_hash,
+commitment_hash_from_merkle_roots), helpers and constants, and registers the same
 ``torch.ops.pearl_gemm.*`` schemas.
 """
 
@@ -22,8 +23,10 @@ from .helpers import (
 )
 from . import pearl_gemm_interface
 from .pearl_gemm_interface import (
+    commitment_hash_from_merkle_roots,
     denoise_converter,
     gemm,
+    get_required_scratchpad_bytes,
     inner_hash,
     kEALScaleFactorDenoise,
     kEBRScaleFactorDenoise,
@@ -32,6 +35,7 @@ from .pearl_gemm_interface import (
     noise_B,
     noise_gen,
     noisy_gemm,
+    tensor_hash,
 )
 from . import ops  # noqa: F401  (registers torch.ops.pearl_gemm.*)
 
@@ -40,6 +44,9 @@ __all__ = [
     "HostSignalHeaderPinnedPool",
     "HostSignalStatus",
     "ProofTileIndices",
+    "commitment_hash_from_merkle_roots",
+    "get_required_scratchpad_bytes",
+    "tensor_hash",
     "denoise_converter",
     "extract_indices",
     "gemm",

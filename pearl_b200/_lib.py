@@ -31,7 +31,8 @@ EXPORTED = [
     "pb2_host_signal_header_size", "pb2_host_signal_sync_size", "pb2_status_string",
     "pb2_last_cuda_error", "pb2_abi_version", "pb2_noise_gen", "pb2_noise_A", "pb2_noise_B",
     "pb2_denoise_converter", "pb2_noisy_gemm", "pb2_gemm", "pb2_inner_hash",
-    "pb2_noisy_gemm_static_scratch",
+    "pb2_noisy_gemm_static_scratch", "pb2_tensor_hash", "pb2_required_scratchpad_bytes",
+    "pb2_commitment_hash_from_merkle_roots",
 ]
 
 _vp = ctypes.c_void_p
@@ -78,6 +79,18 @@ class GemmParams(ctypes.Structure):
                 ("hits", _vp), ("hit_capacity", _i64), ("transcripts", _vp), ("digests", _vp)]
 
 
+class TensorHashParams(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int), ("data", _vp), ("len", _i64), ("key", _vp), ("out", _vp),
+                ("roots", _vp), ("roots_bytes", _i64), ("threads_per_block", ctypes.c_int)]
+
+
+class CommitmentParams(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int), ("A_merkle_root", _vp), ("B_merkle_root", _vp),
+                ("key", _vp), ("A_commitment_hash", _vp), ("B_commitment_hash", _vp),
+                ("routing_root", _vp), ("offsets_hash", _vp), ("salted", ctypes.c_int),
+                ("salted_dim_a", ctypes.c_uint32), ("salted_dim_b", ctypes.c_uint32)]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -96,11 +109,14 @@ def load() -> ctypes.CDLL:
                 "`python -m pearl_b200.build` (there is no CPU fallback)")
         L = ctypes.CDLL(LIB_PATH)
         for name in ("pb2_noise_gen", "pb2_noise_A", "pb2_noise_B", "pb2_denoise_converter",
-                     "pb2_noisy_gemm", "pb2_gemm", "pb2_noisy_gemm_static_scratch"):
+                     "pb2_noisy_gemm", "pb2_gemm", "pb2_noisy_gemm_static_scratch",
+                     "pb2_tensor_hash", "pb2_commitment_hash_from_merkle_roots"):
             getattr(L, name).restype = ctypes.c_int
             getattr(L, name).argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         L.pb2_inner_hash.restype = ctypes.c_int
         L.pb2_inner_hash.argtypes = [ctypes.c_int, _vp, _i64, _vp, _i64, _vp]
+        L.pb2_required_scratchpad_bytes.restype = _i64
+        L.pb2_required_scratchpad_bytes.argtypes = [_i64, ctypes.c_int]
         L.pb2_host_signal_header_size.restype = _i64
         L.pb2_host_signal_sync_size.restype = _i64
         L.pb2_status_string.restype = ctypes.c_char_p

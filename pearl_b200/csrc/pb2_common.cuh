@@ -468,6 +468,34 @@ __device__ __forceinline__ void b3_round(uint32_t* v, const uint32_t* m) {
 }
 #undef PB2_B3_G
 
+constexpr uint32_t kB3Parent = 4;
+
+// out[0..8) = first half of compress(cv, m, counter, block_len, flags): the
+// chaining value (or, with ROOT, the 32-byte hash).
+__device__ __forceinline__ void b3_compress8_at(const uint32_t* cv, const uint32_t* m, uint64_t counter,
+                                                uint32_t block_len, uint32_t flags, uint32_t* out) {
+  uint32_t v[16];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = cv[i];
+  v[8] = kB3IV0;
+  v[9] = kB3IV1;
+  v[10] = kB3IV2;
+  v[11] = kB3IV3;
+  v[12] = uint32_t(counter);
+  v[13] = uint32_t(counter >> 32);
+  v[14] = block_len;
+  v[15] = flags;
+  b3_round<0>(v, m);
+  b3_round<1>(v, m);
+  b3_round<2>(v, m);
+  b3_round<3>(v, m);
+  b3_round<4>(v, m);
+  b3_round<5>(v, m);
+  b3_round<6>(v, m);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) out[i] = v[i] ^ v[i + 8];
+}
+
 // out[0..8) = first half of compress(cv, m, counter=0, block_len=64, flags).
 __device__ __forceinline__ void b3_compress8(const uint32_t* cv, const uint32_t* m,
                                              uint32_t flags, uint32_t* out) {

@@ -59,7 +59,30 @@ SCHEMAS = {
         "Tensor(EBR_fp16!)? EBR_fp16 = None, Tensor? key_A = None, Tensor? key_B = None, "
         "Tensor(aux_buffer!)? aux_buffer = None) -> ()"),
     "inner_hash": "inner_hash(Tensor input_buffer, int iterations = 1) -> Tensor",
+    "tensor_hash": (
+        "tensor_hash(Tensor data, Tensor key, Tensor(out!) out, Tensor(roots!) roots, "
+        "int num_threads = 128, int num_stages = 2, int leaves_per_mt_block = 512) -> ()"),
+    "commitment_hash_from_merkle_roots": (
+        "commitment_hash_from_merkle_roots(Tensor A_merkle_root, Tensor B_merkle_root, Tensor key, "
+        "Tensor(A_commitment_hash!) A_commitment_hash, Tensor(B_commitment_hash!) B_commitment_hash, "
+        "Tensor? routing_root=None, Tensor? offsets_hash=None, int? salted_dim_a=None, "
+        "int? salted_dim_b=None) -> ()"),
 }
+
+
+def _tensor_hash_op(data, key, out, roots, num_threads=128, num_stages=2, leaves_per_mt_block=512):
+    I.tensor_hash(data, key, out, roots, num_threads, num_stages, leaves_per_mt_block)
+
+
+def _commitment_op(A_merkle_root, B_merkle_root, key, A_commitment_hash, B_commitment_hash,
+                   routing_root=None, offsets_hash=None, salted_dim_a=None, salted_dim_b=None):
+    if (salted_dim_a is None) != (salted_dim_b is None):
+        raise RuntimeError("salted_dim_a and salted_dim_b must be provided together")
+    dims = None if salted_dim_a is None else (salted_dim_a, salted_dim_b)
+    I.commitment_hash_from_merkle_roots(A_merkle_root, B_merkle_root, key, A_commitment_hash,
+                                        B_commitment_hash, routing_root, offsets_hash,
+                                        salted_dims=dims)
+
 
 _IMPLS = {
     "noisy_gemm": I.noisy_gemm,
@@ -69,7 +92,13 @@ _IMPLS = {
     "denoise_converter": I.denoise_converter,
     "noise_gen": I.noise_gen,
     "inner_hash": I.inner_hash,
+    "tensor_hash": _tensor_hash_op,
+    "commitment_hash_from_merkle_roots": _commitment_op,
 }
+
+# The reference registers these without the pt2_compliant tag
+# (pearl_gemm_api.cpp:1207-1224).
+_UNTAGGED = ("inner_hash", "tensor_hash", "commitment_hash_from_merkle_roots")
 
 _TAGS = (torch.Tag.pt2_compliant_tag,)
 _lib = None
@@ -84,7 +113,7 @@ def _register() -> None:
         _LOG.warning("torch.ops.pearl_gemm already defined; not registering B200 ops (%s)", e)
         return
     for name, schema in SCHEMAS.items():
-        lib.define(schema, tags=() if name == "inner_hash" else _TAGS)
+        lib.define(schema, tags=() if name in _UNTAGGED else _TAGS)
         lib.impl(name, _IMPLS[name], "CUDA")
     for name in SCHEMAS:
         if name == "inner_hash":

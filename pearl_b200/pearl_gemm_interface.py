@@ -511,6 +511,131 @@ def noisy_gemm(
         _lib.call("pb2_noisy_gemm", p, _stream(A.device), "noisy_gemm")
 
 
+# ------------------------------------------------------------- tensor_hash --
+DEFAULT_THREADS_PER_BLOCK = 128  # tensor_hash_api.hpp:21-23
+DEFAULT_NUM_STAGES = 2
+DEFAULT_LEAVES_PER_MT_BLOCK = 512
+BLAKE3_CHAINING_VALUE_SIZE = 32
+
+
+def get_required_scratchpad_bytes(matrix_bytes: int,
+                                  threads_per_block: int = DEFAULT_THREADS_PER_BLOCK) -> int:
+    """Scratch bytes tensor_hash needs for a tensor of ``matrix_bytes`` bytes:
+    one 32-byte subtree root per ``threads_per_block`` KiB chunks
+    (tensor_hash_api.hpp:37-43)."""
+    return int(_lib.load().pb2_required_scratchpad_bytes(int(matrix_bytes), int(threads_per_block)))
+
+
+def tensor_hash(
+    data,
+    key,
+    out,
+    roots,
+    threads_per_block=DEFAULT_THREADS_PER_BLOCK,
+    num_stages=DEFAULT_NUM_STAGES,
+    leaves_per_mt_block=DEFAULT_LEAVES_PER_MT_BLOCK,
+):
+    """out = BLAKE3 keyed by ``key`` of ``data``'s bytes zero-padded to whole
+    1 KiB chunks; ``roots`` is scratch of at least
+    get_required_scratchpad_bytes(data.numel(), threads_per_block) bytes
+    (tensor_hash_api.hpp:45-120; pearl_gemm_interface.py:550-578).
+    ``num_stages`` and ``leaves_per_mt_block`` are validated like the
+    reference's tuning knobs but select nothing here."""
+    for t, name in ((data, "data"), (key, "key"), (out, "out"), (roots, "roots")):
+        if not t.is_cuda:
+            _fail(f"{name} must be on CUDA")
+        if not t.is_contiguous():
+            _fail(f"{name} must be contiguous")
+    if key.dtype != torch.uint8:
+        _fail("key must be uint8")
+    if out.dtype != torch.uint8:
+        _fail("out must be uint8")
+    if roots.dtype != torch.uint8:
+        _fail("roots must be uint8")
+    if data.dim() != 2:
+        _fail("data must be 2D tensor")
+    if data.data_ptr() % 16 != 0:
+        _fail("data must be 16-byte aligned for TMA")
+    if key.numel() != KEY_LEN:
+        _fail(f"key must have exactly{KEY_LEN}bytes")
+    if out.numel() != BLAKE3_CHAINING_VALUE_SIZE:
+        _fail(f"out must have exactly{BLAKE3_CHAINING_VALUE_SIZE}bytes")
+    if roots.numel() % BLAKE3_CHAINING_VALUE_SIZE != 0:
+        _fail(f"roots must have a multiple of{BLAKE3_CHAINING_VALUE_SIZE}bytes")
+    if threads_per_block not in (128, 256, 512):
+        _fail("threads_per_block must be 128, 256, or 512")
+    if num_stages not in (2, 3, 4):
+        _fail("num_stages must be 2, 3, or 4")
+    if leaves_per_mt_block not in (256, 512, 1024):
+        _fail("leaves_per_mt_block must be 256, 512, or 1024")
+    nbytes = data.numel() * data.element_size()
+    need = get_required_scratchpad_bytes(nbytes, threads_per_block)
+    if roots.numel() < need:
+        _fail(f"roots must have at least {need // 32} * {BLAKE3_CHAINING_VALUE_SIZE}bytes")
+    if nbytes == 0:
+        _fail("data must be non-empty")
+    p = _lib.TensorHashParams()
+    p.device = _device_index(data)
+    p.data, p.len, p.key, p.out = data.data_ptr(), nbytes, key.data_ptr(), out.data_ptr()
+    p.roots, p.roots_bytes, p.threads_per_block = roots.data_ptr(), roots.numel(), threads_per_block
+    with torch.cuda.device(data.device):
+        _lib.call("pb2_tensor_hash", p, _stream(data.device), "tensor_hash")
+
+
+def commitment_hash_from_merkle_roots(
+    A_merkle_root,
+    B_merkle_root,
+    key,
+    A_commitment_hash,
+    B_commitment_hash,
+    routing_root=None,
+    offsets_hash=None,
+    *,
+    salted_dims: tuple[int, int] | None,
+):
+    """Noise seeds from the two tensor roots (tensor_hash_api.hpp:124-212;
+    pearl_gemm_interface.py:581-608): ``salted_dims=(m, n)`` for V3 salted
+    seeds, ``None`` for the legacy chain; ``routing_root`` and
+    ``offsets_hash`` (MoE) fold the routing commitment into A's root."""
+    named = [(A_merkle_root, "A_merkle_root"), (B_merkle_root, "B_merkle_root"), (key, "key"),
+             (A_commitment_hash, "A_commitment_hash"), (B_commitment_hash, "B_commitment_hash")]
+    for t, name in named:
+        if name in ("A_merkle_root", "B_merkle_root", "key") and not t.is_cuda:
+            _fail(f"{name} must be on CUDA")
+        if not t.is_contiguous():
+            _fail(f"{name} must be contiguous")
+        if t.dtype != torch.uint8:
+            _fail(f"{name} must be uint8")
+        if t.numel() != BLAKE3_CHAINING_VALUE_SIZE:
+            _fail(f"{name} must have exactly{BLAKE3_CHAINING_VALUE_SIZE}bytes")
+    if (routing_root is None) != (offsets_hash is None):
+        _fail("routing_root and offsets_hash must be provided together")
+    for t, name in ((routing_root, "routing_root"), (offsets_hash, "offsets_hash")):
+        if t is None:
+            continue
+        if not t.is_cuda:
+            _fail(f"{name} must be on CUDA")
+        if not t.is_contiguous():
+            _fail(f"{name} must be contiguous")
+        if t.dtype != torch.uint8:
+            _fail(f"{name} must be uint8")
+        if t.numel() != BLAKE3_CHAINING_VALUE_SIZE:
+            _fail(f"{name} must have exactly{BLAKE3_CHAINING_VALUE_SIZE}bytes")
+    p = _lib.CommitmentParams()
+    p.device = _device_index(A_merkle_root)
+    p.A_merkle_root, p.B_merkle_root, p.key = _ptr(A_merkle_root), _ptr(B_merkle_root), _ptr(key)
+    p.A_commitment_hash, p.B_commitment_hash = _ptr(A_commitment_hash), _ptr(B_commitment_hash)
+    p.routing_root, p.offsets_hash = _ptr(routing_root), _ptr(offsets_hash)
+    if salted_dims is not None:
+        for d, name in zip(salted_dims, ("salted_dim_a", "salted_dim_b")):
+            if not 0 < int(d) <= 0xFFFFFFFF:
+                _fail(f"{name} must be in [1, {0xFFFFFFFF}], got {d}")
+        p.salted, p.salted_dim_a, p.salted_dim_b = 1, int(salted_dims[0]), int(salted_dims[1])
+    with torch.cuda.device(A_merkle_root.device):
+        _lib.call("pb2_commitment_hash_from_merkle_roots", p, _stream(A_merkle_root.device),
+                  "commitment_hash_from_merkle_roots")
+
+
 # ------------------------------------------------------------ test helpers --
 def inner_hash(input_buffer: torch.Tensor, iterations: int = 1) -> torch.Tensor:
     """XOR of a 64..256-word uint32 buffer, added up ``iterations`` times

@@ -56,7 +56,8 @@ def _c_sizeof(struct: str) -> int:
 
 @pytest.mark.parametrize("cname,pyname", [
     ("pb2_noise_gen_params", "NoiseGenParams"), ("pb2_noising_params", "NoisingParams"),
-    ("pb2_denoise_converter_params", "DenoiseConverterParams"), ("pb2_gemm_params", "GemmParams")])
+    ("pb2_denoise_converter_params", "DenoiseConverterParams"), ("pb2_gemm_params", "GemmParams"),
+    ("pb2_tensor_hash_params", "TensorHashParams"), ("pb2_commitment_params", "CommitmentParams")])
 def test_param_struct_layout_matches_header(cname, pyname):
     assert _c_sizeof(cname) == ctypes.sizeof(getattr(_lib, pyname))
 
@@ -133,3 +134,19 @@ def test_pinned_pool_and_extract_indices():
     idx = pg.extract_indices(h)
     assert idx.A_row_indices == [3 * 128 + 16, 3 * 128 + 24]
     assert idx.B_column_indices == sorted(2 * 256 + 4 + d + 8 * j for j in range(32) for d in (0, 1))
+
+
+def test_required_scratchpad_bytes_formula():
+    # tensor_hash_api.hpp:37-43: one 32-byte root per threads_per_block KiB.
+    for nbytes, tpb in [(1, 128), (128 * 1024, 128), (128 * 1024 + 1, 128), (8192 * 8192, 128),
+                        (10 ** 6, 256), (3 * 512 * 1024, 512)]:
+        want = -(-nbytes // (tpb * 1024)) * 32
+        assert pg.get_required_scratchpad_bytes(nbytes, tpb) == want
+
+
+def test_tensor_hash_and_commitment_validation_on_cpu_tensors():
+    key = torch.zeros(32, dtype=torch.uint8)
+    with pytest.raises(RuntimeError, match="must be on CUDA"):
+        pg.tensor_hash(torch.zeros(4, 4, dtype=torch.uint8), key, key.clone(), key.clone())
+    with pytest.raises(RuntimeError, match="must be on CUDA"):
+        pg.commitment_hash_from_merkle_roots(key, key, key, key.clone(), key.clone(), salted_dims=None)
