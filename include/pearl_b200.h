@@ -110,6 +110,52 @@ typedef struct pb2_commitment_params {
 } pb2_commitment_params;
 PB2_API int pb2_commitment_hash_from_merkle_roots(const pb2_commitment_params* p, void* stream);
 
+/* ---------------------------------------------------- build_routing_data ---
+ * Replaces build_routing_data (miner/pearl-gemm/csrc/moe/build_routing_data.cu:
+ * 40-166): for the (num_tokens, top_k) int32 expert ids, slot_indices = flat
+ * slot indices stably sorted by expert id (8-bit ids, num_experts <= 256),
+ * routing_data = slot_indices / top_k, routing_offsets[e] = number of slots
+ * with expert id <= e.  scratchpad: at least
+ * pb2_build_routing_data_scratchpad_bytes(num_tokens * top_k) bytes, 4-byte
+ * aligned. */
+typedef struct pb2_routing_params {
+  int device;
+  const int32_t* topk_ids; /* (num_tokens, top_k) */
+  int64_t num_tokens, top_k;
+  int32_t* routing_data;    /* (num_tokens * top_k) */
+  int32_t* slot_indices;    /* (num_tokens * top_k) */
+  int32_t* routing_offsets; /* (num_experts) */
+  int64_t num_experts;
+  void* scratchpad;
+  int64_t scratchpad_bytes;
+} pb2_routing_params;
+PB2_API int pb2_build_routing_data(const pb2_routing_params* p, void* stream);
+/* Replaces get_build_routing_data_scratchpad_bytes (build_routing_data.cu:113-125). */
+PB2_API int64_t pb2_build_routing_data_scratchpad_bytes(int64_t numel);
+
+/* -------------------------------------------------------------- quantize ---
+ * Replaces pearl_gemm.quantization.quantize (hadamard.py:530-611), the
+ * activation quantization the mining layer runs before the GEMM
+ * (quantization_operators.py:72-100): per row of x (m, n) bf16 or fp16,
+ * optional block Walsh-Hadamard transform of width block_size (0 = none; else
+ * a power of two in [8, 256] dividing n), times smooth (1 x n, or m x n when
+ * smooth_per_row; may be NULL), then xq = rint(v * max_val / amax) clamped to
+ * +-max_val and scales[row] = amax / max_val.  n % 8 == 0; x and smooth
+ * 16-byte aligned, xq 8-byte aligned. */
+typedef struct pb2_quant_params {
+  int device;
+  const void* x;
+  int x_is_fp16; /* 0: bfloat16 */
+  int64_t m, n;
+  const float* smooth;
+  int smooth_per_row;
+  int8_t* xq;
+  float* scales; /* (m) */
+  int max_val;   /* 63 (7-bit) or 127 (8-bit) */
+  int block_size;
+} pb2_quant_params;
+PB2_API int pb2_quantize(const pb2_quant_params* p, void* stream);
+
 /* ------------------------------------------------------------- noise_gen ---
  * Replaces noise_gen (pearl_gemm_api.cpp:168-298; kernel
  * noise_generation_kernel.h:88-758).  Any output may be NULL (not produced).

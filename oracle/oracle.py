@@ -239,6 +239,20 @@ def tensor_hash(data: np.ndarray, key: bytes) -> bytes:
     return out.tobytes()
 
 
+# ---------------------------------------------------------------- routing ---
+def routing_order(topk_ids: np.ndarray, num_experts: int):
+    """(routing_data, slot_indices, routing_offsets) of build_routing_data
+    (miner/pearl-gemm/csrc/moe/build_routing_data.cu:40-77): flat slots
+    stably sorted by 8-bit expert id, their tokens, and per-expert exclusive
+    ends."""
+    ids = np.ascontiguousarray(topk_ids, np.int64)
+    top_k = ids.shape[1]
+    keys = ids.reshape(-1) & 0xFF
+    slots = np.argsort(keys, kind="stable").astype(np.int32)
+    offsets = np.array([(keys <= e).sum() for e in range(num_experts)], np.int32)
+    return (slots // top_k).astype(np.int32), slots, offsets
+
+
 def num_threads() -> int:
     return lib().po_num_threads()
 

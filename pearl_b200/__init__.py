@@ -37,6 +37,7 @@ from .pearl_gemm_interface import (
     noisy_gemm,
     tensor_hash,
 )
+from . import moe
 from . import ops  # noqa: F401  (registers torch.ops.pearl_gemm.*)
 
 __all__ = [
@@ -55,6 +56,7 @@ __all__ = [
     "get_host_signal_sync_fields",
     "get_host_signal_sync_size",
     "inner_hash",
+    "moe",
     "kEALScaleFactorDenoise",
     "kEBRScaleFactorDenoise",
     "make_pow_target_tensor",

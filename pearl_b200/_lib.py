@@ -32,7 +32,8 @@ EXPORTED = [
     "pb2_last_cuda_error", "pb2_abi_version", "pb2_noise_gen", "pb2_noise_A", "pb2_noise_B",
     "pb2_denoise_converter", "pb2_noisy_gemm", "pb2_gemm", "pb2_inner_hash",
     "pb2_noisy_gemm_static_scratch", "pb2_tensor_hash", "pb2_required_scratchpad_bytes",
-    "pb2_commitment_hash_from_merkle_roots",
+    "pb2_commitment_hash_from_merkle_roots", "pb2_build_routing_data",
+    "pb2_build_routing_data_scratchpad_bytes", "pb2_quantize",
 ]
 
 _vp = ctypes.c_void_p
@@ -91,6 +92,18 @@ class CommitmentParams(ctypes.Structure):
                 ("salted_dim_a", ctypes.c_uint32), ("salted_dim_b", ctypes.c_uint32)]
 
 
+class RoutingParams(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int), ("topk_ids", _vp), ("num_tokens", _i64), ("top_k", _i64),
+                ("routing_data", _vp), ("slot_indices", _vp), ("routing_offsets", _vp),
+                ("num_experts", _i64), ("scratchpad", _vp), ("scratchpad_bytes", _i64)]
+
+
+class QuantParams(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int), ("x", _vp), ("x_is_fp16", ctypes.c_int), ("m", _i64),
+                ("n", _i64), ("smooth", _vp), ("smooth_per_row", ctypes.c_int), ("xq", _vp),
+                ("scales", _vp), ("max_val", ctypes.c_int), ("block_size", ctypes.c_int)]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -110,11 +123,14 @@ def load() -> ctypes.CDLL:
         L = ctypes.CDLL(LIB_PATH)
         for name in ("pb2_noise_gen", "pb2_noise_A", "pb2_noise_B", "pb2_denoise_converter",
                      "pb2_noisy_gemm", "pb2_gemm", "pb2_noisy_gemm_static_scratch",
-                     "pb2_tensor_hash", "pb2_commitment_hash_from_merkle_roots"):
+                     "pb2_tensor_hash", "pb2_commitment_hash_from_merkle_roots",
+                     "pb2_build_routing_data", "pb2_quantize"):
             getattr(L, name).restype = ctypes.c_int
             getattr(L, name).argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         L.pb2_inner_hash.restype = ctypes.c_int
         L.pb2_inner_hash.argtypes = [ctypes.c_int, _vp, _i64, _vp, _i64, _vp]
+        L.pb2_build_routing_data_scratchpad_bytes.restype = _i64
+        L.pb2_build_routing_data_scratchpad_bytes.argtypes = [_i64]
         L.pb2_required_scratchpad_bytes.restype = _i64
         L.pb2_required_scratchpad_bytes.argtypes = [_i64, ctypes.c_int]
         L.pb2_host_signal_header_size.restype = _i64

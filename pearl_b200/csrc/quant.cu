@@ -1,0 +1,170 @@
+// quant.cu -- per-token symmetric quantization of the activations that feed
+// a mined GEMM: the caller step quant_7bit / quant_8bit of
+// miner/vllm-miner/src/vllm_miner/quantization_operators.py:72-100, which
+// runs pearl_gemm.quantization.quantize (hadamard.py:530-611).
+//
+// Per row: x (bf16 / fp16) -> optional block-diagonal Walsh-Hadamard
+// transform of width k (Sylvester order, scaled by 1/sqrt(k), first element
+// of every block negated: hadamard.py:476-517) -> times the smooth scale ->
+// amax; scale = amax / max_val, q = rint(x * max_val / (amax + 1e-30))
+// clamped to [-max_val, max_val] (hadamard.py:443-466).
+//
+// One 256-thread CTA per row, eight elements per thread and 16-byte loads:
+// a k-block is k/8 consecutive threads of one warp, so the cross-element
+// butterflies are register and shuffle work.  Two passes over the row (amax,
+// then quantize); the second pass re-reads the row from L1/L2.  HBM-bound:
+// 2 bytes read and 1 written per element.
+#include <cuda_bf16.h>
+
+#include <cmath>
+
+#include "pb2_common.cuh"
+
+namespace pb2 {
+namespace {
+
+constexpr int kQuantThreads = 256;
+
+struct QuantArgs {
+  const void* x;
+  const float* smooth;
+  int smooth_per_row;
+  int8_t* xq;
+  float* scales;
+  int m, n;
+  int block;   // Hadamard width, 0 = none
+  float norm;  // 1/sqrt(block), correctly rounded (the reference's constant)
+  float max_val;
+};
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+
+// Loads vector `vec` (8 elements) of `row`, applies the Hadamard transform of
+// width a.block and the smooth scale.  Every lane of the warp must call it
+// with the same `iter` (the butterflies shuffle across lanes).
+template <typename T>
+__device__ __forceinline__ void load_vec(const QuantArgs& a, int row, int vec, bool valid, float* v) {
+  if (valid) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(static_cast<const T*>(a.x) + int64_t(row) * a.n + 8 * vec);
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = to_f32<T>(e[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+  }
+  if (a.block > 0) {
+#pragma unroll
+    for (int s = 1; s < 8; s <<= 1) {  // butterflies inside the 8-element vector
+      float w[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[i] = (i & s) ? v[i ^ s] - v[i] : v[i] + v[i ^ s];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = w[i];
+    }
+    const int lane = threadIdx.x & 31;
+    for (int s = 1; 8 * s < a.block; s <<= 1) {  // butterflies across the block's lanes
+      const bool upper = lane & s;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float other = __shfl_xor_sync(0xffffffffu, v[i], s);
+        v[i] = upper ? other - v[i] : v[i] + other;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] *= a.norm;
+    if (vec % (a.block / 8) == 0) v[0] = -v[0];  // first element of the block
+  }
+  if (a.smooth && valid) {
+    const float* sp = a.smooth + (a.smooth_per_row ? int64_t(row) * a.n : 0) + 8 * vec;
+    const float4 s0 = *reinterpret_cast<const float4*>(sp);
+    const float4 s1 = *reinterpret_cast<const float4*>(sp + 4);
+    v[0] *= s0.x; v[1] *= s0.y; v[2] *= s0.z; v[3] *= s0.w;
+    v[4] *= s1.x; v[5] *= s1.y; v[6] *= s1.z; v[7] *= s1.w;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const QuantArgs a) {
+  __shared__ float warp_max[kQuantThreads / 32];
+  const int row = blockIdx.x;
+  const int nvec = a.n / 8;
+  const int iters = (nvec + kQuantThreads - 1) / kQuantThreads;
+  float amax = 0.f;
+  for (int it = 0; it < iters; ++it) {
+    const int vec = it * kQuantThreads + threadIdx.x;
+    float v[8];
+    load_vec<T>(a, row, vec, vec < nvec, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x / 32] = amax;
+  __syncthreads();
+  amax = 0.f;
+#pragma unroll
+  for (int w = 0; w < kQuantThreads / 32; ++w) amax = fmaxf(amax, warp_max[w]);
+  const float inv = a.max_val / (amax + 1e-30f);
+  if (threadIdx.x == 0) a.scales[row] = amax * (1.0f / a.max_val);
+  for (int it = 0; it < iters; ++it) {
+    const int vec = it * kQuantThreads + threadIdx.x;
+    float v[8];
+    load_vec<T>(a, row, vec, vec < nvec, v);
+    if (vec < nvec) {
+      uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float q = fminf(fmaxf(rintf(v[i] * inv), -a.max_val), a.max_val);
+        packed[i / 4] |= (uint32_t(int32_t(q)) & 0xFFu) << (8 * (i % 4));
+      }
+      *reinterpret_cast<uint2*>(a.xq + int64_t(row) * a.n + 8 * vec) = make_uint2(packed[0], packed[1]);
+    }
+  }
+}
+
+}  // namespace
+}  // namespace pb2
+
+extern "C" int pb2_quantize(const pb2_quant_params* pp, void* stream) {
+  using namespace pb2;
+  if (!pp) return PB2_ERR_INVALID_ARGUMENT;
+  const pb2_quant_params& p = *pp;
+  if (p.m < 0 || p.n <= 0 || p.m > INT32_MAX || p.n > INT32_MAX) return PB2_ERR_INVALID_ARGUMENT;
+  if (!p.x || !p.xq || !p.scales || p.max_val <= 0 || p.max_val > 127) return PB2_ERR_INVALID_ARGUMENT;
+  if (p.n % 8 != 0) return PB2_ERR_UNSUPPORTED_CONFIG;  // 16-byte row vectors
+  if (p.block_size != 0) {
+    const int k = p.block_size;
+    // Blocks span whole 8-element vectors of one warp (the reference's
+    // layout: hadamard.py:556-571).
+    if (k < 8 || (k & (k - 1)) != 0 || k > 256 || p.n % k != 0) return PB2_ERR_UNSUPPORTED_CONFIG;
+  }
+  if (reinterpret_cast<uintptr_t>(p.x) % 16 || reinterpret_cast<uintptr_t>(p.xq) % 8 ||
+      (p.smooth && reinterpret_cast<uintptr_t>(p.smooth) % 16))
+    return PB2_ERR_INVALID_ARGUMENT;
+  int st = set_device(p.device);
+  if (st) return st;
+  if (p.m == 0) return PB2_OK;
+  QuantArgs a;
+  a.x = p.x;
+  a.smooth = p.smooth;
+  a.smooth_per_row = p.smooth_per_row;
+  a.xq = p.xq;
+  a.scales = p.scales;
+  a.m = int(p.m);
+  a.n = int(p.n);
+  a.block = p.block_size;
+  a.norm = p.block_size ? float(1.0 / sqrt(double(p.block_size))) : 1.0f;
+  a.max_val = float(p.max_val);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p.x_is_fp16)
+    quant_rows_kernel<__half><<<a.m, kQuantThreads, 0, s>>>(a);
+  else
+    quant_rows_kernel<__nv_bfloat16><<<a.m, kQuantThreads, 0, s>>>(a);
+  return launch_status();
+}

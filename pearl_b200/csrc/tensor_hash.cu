@@ -59,10 +59,11 @@ __device__ __forceinline__ void load_block(const TensorHashArgs& a, uint64_t c, 
       m[4 * j + 2] = q.z;
       m[4 * j + 3] = q.w;
     }
-  } else {
-#pragma unroll 1
+  } else {  // the ragged end of the data (unrolled: m stays in registers)
+#pragma unroll
     for (int w = 0; w < 16; ++w) {
       uint32_t word = 0;
+#pragma unroll
       for (int i = 0; i < 4; ++i) {
         const uint64_t idx = off + 4 * w + i;
         if (idx < a.len) word |= uint32_t(a.data[idx]) << (8 * i);
@@ -77,10 +78,15 @@ __device__ void chunk_cv(const TensorHashArgs& a, const uint32_t* key, uint64_t 
                          uint32_t* cv) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) cv[i] = key[i];
+  // Block b + 1 is loaded before block b is compressed, so its latency hides
+  // behind the compression (a warp per SM sub-partition is all a 64 MiB
+  // tensor offers: one thread per chunk, sixteen dependent compressions).
+  uint32_t m[16];
+  load_block(a, c, 0, m);
 #pragma unroll 1
   for (int b = 0; b < kChunkBytes / 64; ++b) {
-    uint32_t m[16];
-    load_block(a, c, b, m);
+    uint32_t mn[16];
+    if (b + 1 < kChunkBytes / 64) load_block(a, c, b + 1, mn);
     uint32_t flags = kB3Keyed;
     if (b == 0) flags |= kB3ChunkStart;
     if (b == kChunkBytes / 64 - 1) flags |= kB3ChunkEnd | (root ? kB3Root : 0u);
@@ -88,6 +94,10 @@ __device__ void chunk_cv(const TensorHashArgs& a, const uint32_t* key, uint64_t 
     b3_compress8_at(cv, m, c, 64, flags, next);
 #pragma unroll
     for (int i = 0; i < 8; ++i) cv[i] = next[i];
+    if (b + 1 < kChunkBytes / 64) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) m[i] = mn[i];
+    }
   }
 }
 

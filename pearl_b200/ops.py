@@ -13,6 +13,7 @@ import logging
 
 import torch
 
+from . import moe as M
 from . import pearl_gemm_interface as I
 
 _LOG = logging.getLogger(__name__)
@@ -67,6 +68,10 @@ SCHEMAS = {
         "Tensor(A_commitment_hash!) A_commitment_hash, Tensor(B_commitment_hash!) B_commitment_hash, "
         "Tensor? routing_root=None, Tensor? offsets_hash=None, int? salted_dim_a=None, "
         "int? salted_dim_b=None) -> ()"),
+    "build_routing_data": (
+        "build_routing_data(Tensor topk_ids, Tensor(routing_data!) routing_data, "
+        "Tensor(slot_indices!) slot_indices, Tensor(routing_offsets!) routing_offsets, "
+        "Tensor(scratchpad!) scratchpad, int num_experts) -> ()"),
 }
 
 
@@ -94,11 +99,12 @@ _IMPLS = {
     "inner_hash": I.inner_hash,
     "tensor_hash": _tensor_hash_op,
     "commitment_hash_from_merkle_roots": _commitment_op,
+    "build_routing_data": M.build_routing_data,
 }
 
 # The reference registers these without the pt2_compliant tag
 # (pearl_gemm_api.cpp:1207-1224).
-_UNTAGGED = ("inner_hash", "tensor_hash", "commitment_hash_from_merkle_roots")
+_UNTAGGED = ("inner_hash", "tensor_hash", "commitment_hash_from_merkle_roots", "build_routing_data")
 
 _TAGS = (torch.Tag.pt2_compliant_tag,)
 _lib = None
