@@ -117,17 +117,20 @@ def setup_dist(args):
 # ------------------------------------------------------------------ ours ---
 def run_ours(args, world, rank, local):
     import pearl_b200 as pg
+    from pearl_b200 import shard
     from tests.gpu_problem import make_problem, signal_buffers
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     p = make_problem(M, N, K, R, seed=1000 + rank, device=dev)
-    # A fresh pair of noise seeds every step (distinct points of the nonce
-    # space), all resident on the device before timing.
+    # A fresh pair of noise seeds every step: every rank mines its own points
+    # of the nonce space (shard.rank_job_key), all resident before timing.
     n_keys = args.warmup + args.steps
-    g = torch.Generator().manual_seed(97 + rank)
-    keys_a = torch.randint(0, 256, (n_keys, 32), dtype=torch.uint8, generator=g).to(dev)
-    keys_b = torch.randint(0, 256, (n_keys, 32), dtype=torch.uint8, generator=g).to(dev)
+    base = bytes(range(32))
+    keys_a = torch.tensor([list(shard.rank_job_key(base, rank, 2 * i)) for i in range(n_keys)],
+                          dtype=torch.uint8).to(dev)
+    keys_b = torch.tensor([list(shard.rank_job_key(base, rank, 2 * i + 1)) for i in range(n_keys)],
+                          dtype=torch.uint8).to(dev)
     target = pg.make_pow_target_tensor(target_value(TARGET_FRACTION), dev)
     header, sync = signal_buffers(dev)
     hits = torch.zeros(1024, 12, dtype=torch.uint32, device=dev)
@@ -179,15 +182,14 @@ def run_ours(args, world, rank, local):
     clk = clocks.stop()
     ms = t0.elapsed_time(t1)
     main_ms = sum(a.elapsed_time(b) for a, b in ev_main) / len(ev_main)
-    total_hits = int(pg.get_host_signal_sync_fields(sync)["hit_count"])
+    local_hits = int(pg.get_host_signal_sync_fields(sync)["hit_count"])
+    total_hits = local_hits
     if world > 1:
-        import torch.distributed as dist
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        h = torch.tensor([total_hits], device=dev)
-        dist.all_reduce(h)
-        total_hits = int(h.item())
+        # The only cross-rank traffic: the slowest rank's time and the
+        # winning proofs, gathered to rank 0 after the timed region.
+        ms = shard.max_over_ranks(ms, dev)
+        gathered = shard.gather_hits(hits, min(local_hits, hits.shape[0]))
+        total_hits = None if gathered is None else int(gathered.shape[0])
 
     # ---- end to end through the public API with host buffers -------------
     e2e = run_e2e(args, p, keys_a, keys_b, target, header, sync, dev, world)
@@ -266,10 +268,13 @@ def barrier(world):
 
 
 def run_e2e(args, p, keys_a, keys_b, target, header, sync, dev, world):
-    """Same metric through the public call a miner makes (noise_gen +
-    noisy_gemm with noising), inputs copied from pinned host memory every step
-    and the step's result (sync word + hit list) read back."""
+    """Same metric through the public calls a miner makes (noise_gen +
+    noisy_gemm with in-kernel noising), with every step's A and B copied from
+    pinned host memory and its result (sync word + hit list) read back, all
+    inside the timed region.  Two device buffer sets let step i+1's copies
+    (on their own stream) overlap step i's GEMM."""
     import pearl_b200 as pg
+    from pearl_b200 import shard
 
     hostA = p.A.cpu().pin_memory()
     hostB = p.B.cpu().pin_memory()
@@ -277,41 +282,60 @@ def run_e2e(args, p, keys_a, keys_b, target, header, sync, dev, world):
     sync_host = torch.zeros(16, dtype=torch.int8).pin_memory()
     hits = torch.zeros(64, 12, dtype=torch.uint32, device=dev)
     stream = torch.cuda.current_stream(dev)
+    copy_stream = torch.cuda.Stream(dev)
+    bufs = [(p.A, p.B), (torch.empty_like(p.A), torch.empty_like(p.B))]
+    copied = [torch.cuda.Event() for _ in bufs]
+    consumed = [torch.cuda.Event() for _ in bufs]
     steps = max(1, min(args.steps, args.e2e_steps))
 
-    def step(i):
-        p.A.copy_(hostA, non_blocking=True)
-        p.B.copy_(hostB, non_blocking=True)
+    def issue_copy(i):
+        b = i % 2
+        if i >= 2:
+            copy_stream.wait_event(consumed[b])  # step i-2 is done with the buffers
+        with torch.cuda.stream(copy_stream):
+            bufs[b][0].copy_(hostA, non_blocking=True)
+            bufs[b][1].copy_(hostB, non_blocking=True)
+            copied[b].record(copy_stream)
+
+    def compute(i):
+        b = i % 2
+        A, B = bufs[b]
+        stream.wait_event(copied[b])
         sync.zero_()
         ka, kb = keys_a[i % len(keys_a)], keys_b[i % len(keys_b)]
         pg.noise_gen(R=R, key_A=ka, key_B=kb, **p.noise)
-        pg.noisy_gemm(A=p.A, B=p.B, A_scales=p.A_scales, B_scales=p.B_scales,
+        pg.noisy_gemm(A=A, B=B, A_scales=p.A_scales, B_scales=p.B_scales,
                       host_signal_header_pinned=header, host_signal_sync=sync, pow_target=target,
                       pow_key=ka.view(torch.uint32), hits=hits, **p.noise, **p.out)
+        consumed[b].record(stream)
         sync_host.copy_(sync, non_blocking=True)
         hit_host.copy_(hits, non_blocking=True)
 
-    for i in range(3):
-        step(i)
+    def run(n):
+        issue_copy(0)
+        for i in range(n):
+            if i + 1 < n:
+                issue_copy(i + 1)
+            compute(i)
+
+    run(3)
     torch.cuda.synchronize(dev)
     barrier(world)
     a, b = torch.cuda.Event(True), torch.cuda.Event(True)
     a.record(stream)
-    for i in range(steps):
-        step(i)
+    copy_stream.wait_event(a)  # the copies belong to the timed region too
+    run(steps)
     b.record(stream)
     torch.cuda.synchronize(dev)
     ms = a.elapsed_time(b)
     if world > 1:
-        import torch.distributed as dist
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms = shard.max_over_ranks(ms, dev)
     step_s = ms / steps * 1e-3
     return {"value": round(world * 2.0 * M * N * K / step_s / 1e12, 2), "unit": "TOPS",
             "h2d_bytes_per_step": 2 * M * K, "d2h_bytes_per_step": 16 + hit_host.numel() * 4,
             "steps": steps, "ms_per_step": round(ms / steps, 4),
-            "path": "pearl_b200.noise_gen + pearl_b200.noisy_gemm (run_noising_A/B) from pinned host A,B"}
+            "path": "pearl_b200.noise_gen + pearl_b200.noisy_gemm (run_noising_A/B) from pinned host A,B; "
+                    "next step's copies overlap this step's GEMM"}
 
 
 # ------------------------------------------------------- CPU reference ----
