@@ -108,36 +108,16 @@ __device__ __forceinline__ uint32_t pack_bf16(float x, float y) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// One fold warp's 32 x 32 block of C (lane = row, v = 32 consecutive
-// accumulator columns of the lane's row): scale, convert to bf16, write the
-// block into the warp's shared-memory box and hand it to a TMA store, which
-// writes whole lines and clips rows >= M and columns >= N.  Writing C straight
-// from registers would scatter every store instruction over 32 rows, and the
-// fold warps would spend thousands of cycles in the store unit while the MMA
-// issuer waits for their next release.
-template <bool kFloatAcc>
-__device__ __forceinline__ void store_c_block(const MainArgs& a, uint8_t* box, const uint32_t* v,
-                                              int row0, int col0, float row_scale, int lane) {
+// One fold warp's 32 x 32 block of C (lane = row, `w` = the row's 32 bf16
+// values as 16 packed pairs): write the block into the warp's shared-memory
+// box and hand it to a TMA store, which writes whole lines and clips rows >= M
+// and columns >= N.  Writing C straight from registers would scatter every
+// store instruction over 32 rows, and the fold warps would spend thousands of
+// cycles in the store unit while the MMA issuer waits for their next release.
+__device__ __forceinline__ void store_c_packed(const MainArgs& a, uint8_t* box, const uint32_t* w,
+                                               int row0, int col0, int lane) {
   if (lane == 0) bulk_wait_read_all();  // the box's previous store has read it
   __syncwarp();
-  const float4* sb = reinterpret_cast<const float4*>(a.sB + col0);
-  uint32_t w[16];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    float4 b0 = make_float4(0.f, 0.f, 0.f, 0.f), b1 = b0;
-    if (col0 + 8 * j < a.N) {  // N % 8 == 0: a group of 8 columns is all in or all out
-      b0 = sb[2 * j];
-      b1 = sb[2 * j + 1];
-    }
-    float f[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      f[i] = kFloatAcc ? __uint_as_float(v[8 * j + i]) : float(int(v[8 * j + i]));
-    w[4 * j + 0] = pack_bf16(f[0] * row_scale * b0.x, f[1] * row_scale * b0.y);
-    w[4 * j + 1] = pack_bf16(f[2] * row_scale * b0.z, f[3] * row_scale * b0.w);
-    w[4 * j + 2] = pack_bf16(f[4] * row_scale * b1.x, f[5] * row_scale * b1.y);
-    w[4 * j + 3] = pack_bf16(f[6] * row_scale * b1.z, f[7] * row_scale * b1.w);
-  }
   // 64-byte swizzle (the tensor map's): 16-byte chunk k of row r sits at
   // chunk k ^ ((r >> 1) & 3), which also spreads a store instruction's 32
   // lanes over all banks.
@@ -461,53 +441,30 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
       const bool do_fold = kReduce && is_main;
       const bool do_convert = kDenoise && last_main;
       const bool do_store = (!kDenoise && last_main) || !is_main;
-      uint32_t v[64];
-      __syncwarp();
-      tmem_ld32(taddr, v);
-      tmem_ld32(taddr + 32, v + 32);
-      tmem_wait_ld();
-      uint32_t p0 = 0, p1 = 0, p2 = 0, p3 = 0;
-      if (do_convert) {
-        // S as f32 * 2^-12 for the f16 denoise MMAs (the fold reads the
-        // integer values first).
-        if (do_fold) {
-#pragma unroll
-          for (int i = 0; i < 64; i += 8) {
-            p0 ^= v[i] ^ v[i + 1];
-            p1 ^= v[i + 2] ^ v[i + 3];
-            p2 ^= v[i + 4] ^ v[i + 5];
-            p3 ^= v[i + 6] ^ v[i + 7];
-          }
+      // The strip is read as two 32-column halves (32 registers each): 64
+      // live accumulators would not fit beside the rest of a fold warp's
+      // state in the 96 registers 20 warps leave per thread, and spilled
+      // registers go to a 29 KB L1 (the rest of the SM's SRAM is shared
+      // memory).  The per-chunk fold and a tile's last events (f32 rewrite,
+      // C) are separate code paths so the hot one stays small.
+      auto release = [&](bool after_store) {
+        // The slot's TMEM traffic is done.  After loads only (drained by
+        // wait::ld) a relaxed arrive suffices, and it never waits for this
+        // warp's C stores still in flight; after the f32 rewrite the arrive
+        // must release the tcgen05.st to the issuer's MMAs (cluster scope:
+        // the peer's stores feed the leader's MMAs).
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (after_store)
+            mbar_arrive_remote(rel_base + 8 * s);
+          else
+            mbar_arrive_relaxed_cluster(rel_base + 8 * s);
         }
-#pragma unroll
-        for (int i = 0; i < 64; ++i) v[i] = __float_as_uint(float(int(v[i])) * (1.0f / 4096.0f));
-        tmem_st32(taddr, v);
-        tmem_st32(taddr + 32, v + 32);
-        tmem_wait_st();
-      }
-      // The slot's TMEM traffic is done: release it before any arithmetic.
-      // After loads only (drained by wait::ld) a relaxed arrive suffices, and
-      // it never waits for this warp's C stores still in flight; after the
-      // f32 rewrite the arrive must release the tcgen05.st to the issuer's
-      // MMAs (cluster scope: the peer's stores feed the leader's MMAs).
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if (do_convert)
-          mbar_arrive_remote(rel_base + 8 * s);
-        else
-          mbar_arrive_relaxed_cluster(rel_base + 8 * s);
-      }
-      if (do_fold && !do_convert) {
-#pragma unroll
-        for (int i = 0; i < 64; i += 8) {
-          p0 ^= v[i] ^ v[i + 1];
-          p1 ^= v[i + 2] ^ v[i + 3];
-          p2 ^= v[i + 4] ^ v[i + 5];
-          p3 ^= v[i + 6] ^ v[i + 7];
-        }
-      }
-      if (do_fold) {
+      };
+      // Pairs rows r and r + 8 and XORs the pre-rotated fold into the tile's
+      // transcript word.
+      auto commit_fold = [&](uint32_t p0, uint32_t p1, uint32_t p2, uint32_t p3) -> bool {
         const uint32_t g0 = __shfl_xor_sync(0xffffffffu, is_low ? p2 : p0, 8);
         const uint32_t g1 = __shfl_xor_sync(0xffffffffu, is_low ? p3 : p1, 8);
         const uint32_t f0 = (is_low ? p0 : p2) ^ g0;
@@ -519,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
         // warps must have cleared it.
         if (u == 0 && round >= 2 &&
             !(ok = mbar_wait_idle(&S.xfree[b], ((round >> 1) - 1) & 1, abort_flag, a.sync)))
-          return;
+          return false;
         uint32_t* tw = xbuf + b * (16 * 256) + w * 256 + lane_tile;
         atomicXor(tw, __funnelshift_l(f0, f0, rot));
         atomicXor(tw + 16, __funnelshift_l(f1, f1, rot));
@@ -530,21 +487,78 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
           __syncwarp();
           if (lane == 0) mbar_arrive(&S.xready[b]);  // this warp's contributions are in
         }
+        return true;
+      };
+      auto fold32 = [](const uint32_t* v, uint32_t& p0, uint32_t& p1, uint32_t& p2, uint32_t& p3) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          p0 ^= v[i] ^ v[i + 1];
+          p1 ^= v[i + 2] ^ v[i + 3];
+          p2 ^= v[i + 4] ^ v[i + 5];
+          p3 ^= v[i + 6] ^ v[i + 7];
+        }
+      };
+
+      if (!do_convert && !do_store) {
+        // ---- every chunk but a tile's last: fold only
+        uint32_t p0 = 0, p1 = 0, p2 = 0, p3 = 0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t v[32];
+          __syncwarp();
+          tmem_ld32(taddr + 32 * h, v);
+          tmem_wait_ld_into(v);
+          fold32(v, p0, p1, p2, p3);
+        }
+        release(false);
+        commit_fold(p0, p1, p2, p3);
+        return;
       }
-      // C last: the transcript is complete and the hash warps can start.
+      // ---- a tile's last chunk (fold + f32 rewrite, or fold + C) or its final C
+      float rs = 0.f;
+      float2 sbv = make_float2(0.f, 0.f);
+      if (do_store) {  // scales first: their latency overlaps the loads
+        const int row = tm * BM + int(rank) * BMC + 32 * q + lane;
+        rs = (row < a.M ? a.sA[row] : 0.0f) * (is_main ? 1.0f : 4096.0f);
+        const int c = tn * BN + 64 * wi + 2 * lane;  // this lane's two column scales
+        if (c < a.N) sbv = *reinterpret_cast<const float2*>(a.sB + c);
+      }
+      uint32_t p0 = 0, p1 = 0, p2 = 0, p3 = 0;
+      uint32_t packed[32];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t v[32];
+        __syncwarp();
+        tmem_ld32(taddr + 32 * h, v);
+        tmem_wait_ld_into(v);
+        if (do_fold) fold32(v, p0, p1, p2, p3);
+        if (do_convert) {
+          // S as f32 * 2^-12 for the f16 denoise MMAs (folded above first).
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(float(int(v[i])) * (1.0f / 4096.0f));
+          tmem_st32(taddr + 32 * h, v);
+        }
+        if (do_store) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const int src = 16 * h + i / 2;  // lane holding columns 32h + i, +1
+            const float bx = __shfl_sync(0xffffffffu, sbv.x, src);
+            const float by = __shfl_sync(0xffffffffu, sbv.y, src);
+            const float f0 = is_main ? float(int(v[i])) : __uint_as_float(v[i]);
+            const float f1 = is_main ? float(int(v[i + 1])) : __uint_as_float(v[i + 1]);
+            packed[16 * h + i / 2] = pack_bf16(f0 * rs * bx, f1 * rs * by);
+          }
+        }
+      }
+      if (do_convert) tmem_wait_st();
+      release(do_convert);
+      if (do_fold && !commit_fold(p0, p1, p2, p3)) return;
       if (do_store) {
         const int row0 = tm * BM + int(rank) * BMC + 32 * q;
-        const int row = row0 + lane;
-        const float sa = row < a.M ? a.sA[row] : 0.0f;
         uint8_t* box = cstage + fw * kCBoxBytes;
         const int col = tn * BN + 64 * wi;
-        if (!is_main) {
-          store_c_block<true>(a, box, v, row0, col, sa * 4096.0f, lane);
-          store_c_block<true>(a, box, v + 32, row0, col + 32, sa * 4096.0f, lane);
-        } else {
-          store_c_block<false>(a, box, v, row0, col, sa, lane);
-          store_c_block<false>(a, box, v + 32, row0, col + 32, sa, lane);
-        }
+        store_c_packed(a, box, packed, row0, col, lane);
+        store_c_packed(a, box, packed + 16, row0, col + 32, lane);
       }
     };
 

@@ -151,6 +151,10 @@ __device__ __forceinline__ void bulk_commit_group() {
 __device__ __forceinline__ void bulk_wait_read_all() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
+// ... all but the most recent group (double-buffered staging).
+__device__ __forceinline__ void bulk_wait_read_all_but_one() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
 // Wait until this thread's bulk stores are complete (written to global).
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
@@ -387,6 +391,19 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* v) {
       : "memory");
 }
 #undef PB2_W8
+
+// tcgen05.wait::ld that also "writes" the 32 registers the loads filled, so
+// the compiler cannot schedule a use of them before the wait (the loads
+// complete asynchronously; their asm statement alone does not say so).
+#define PB2_T8(p, o) "+r"(p[o + 0]), "+r"(p[o + 1]), "+r"(p[o + 2]), "+r"(p[o + 3]), \
+    "+r"(p[o + 4]), "+r"(p[o + 5]), "+r"(p[o + 6]), "+r"(p[o + 7])
+__device__ __forceinline__ void tmem_wait_ld_into(uint32_t* v) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : PB2_T8(v, 0), PB2_T8(v, 8), PB2_T8(v, 16), PB2_T8(v, 24)
+               :
+               : "memory");
+}
+#undef PB2_T8
 
 // TMEM loads/stores, 16 lanes x 256 bit shape, 8 repetitions (64 columns):
 // thread t holds, for repetition j, (lane base + t/4, col 8j + 2(t%4)),
