@@ -428,6 +428,118 @@ def run_reference(args, world, rank):
     }
 
 
+# --------------------------------------------------- other BASELINE configs
+def _time_steps(fn, steps, warmup, dev, world):
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    stream = torch.cuda.current_stream(dev)
+    a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+    a.record(stream)
+    for i in range(steps):
+        fn(warmup + i)
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b)
+    if world > 1:
+        from pearl_b200 import shard
+        ms = shard.max_over_ranks(ms, dev)
+    return ms / steps
+
+
+def _line(args, world, name, ops_per_step, ms, extra, mined_gemms):
+    step_s = ms * 1e-3
+    return {"metric": "effective TOPS (mined int8 noisy GEMM with fused transcript hashing)",
+            "value": round(world * ops_per_step / step_s / 1e12, 2), "unit": "TOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seeded int7 weights / bf16 activations, random routing)",
+            "config": {"workload": name, "mined_gemms_per_step": mined_gemms, **extra},
+            "e2e": None, "cpu_baseline": None}
+
+
+def run_workload(args, world, rank, local):
+    """BASELINE configs 3-5 (the default line is config 2): timed through the
+    operators a miner calls, one step = one pass of the workload."""
+    from pearl_b200 import miner as MN
+    from pearl_b200 import shard
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    g = torch.Generator().manual_seed(77 + rank)
+    base = bytes(range(32))
+    job = lambda i: MN.MiningJob(shard.rank_job_key(base, rank, i), target_value(TARGET_FRACTION))  # noqa: E731
+    if args.workload == "gemm16384":
+        m, n, k = 16384, 8192, 8192
+        A = torch.randint(-64, 64, (m, k), generator=g, dtype=torch.int8).to(dev)
+        B = torch.randint(-64, 64, (n, k), generator=g, dtype=torch.int8).to(dev)
+        sa = torch.full((m,), 1 / 128, device=dev)
+        sb = torch.full((n,), 1 / 128, device=dev)
+        done = []
+
+        def step(i):
+            C, mined = MN.pearl_gemm_noisy(A, B, sa, sb, torch.bfloat16, job(i))
+            done.append(mined)
+            if len(done) > 8:
+                MN.release_header(done.pop(0).host_signal_header_pinned)
+        ms = _time_steps(step, args.steps, args.warmup, dev, world)
+        return _line(args, world, "config 3 shape, int8 path: noisy GEMM M=16384 N=K=8192 with "
+                     "commitment (tensor_hash A,B), noise_gen, noising, transcript, BLAKE3",
+                     2.0 * m * n * k, ms, {"m": m, "n": n, "k": k, "r": R}, 1) if rank == 0 else None
+    if args.workload in ("llama", "llama_decode"):
+        tokens = 8192 if args.workload == "llama" else 256
+        hidden, mlp, layers = 4096, 14336, 32
+        shapes = [("qkv", 6144, hidden), ("o", hidden, hidden), ("gate_up", 2 * mlp, hidden),
+                  ("down", hidden, mlp)]
+
+        class Layer:
+            pass
+        w = {}
+        for name, n_out, k_in in shapes:  # one weight per projection, reused by the 32 layers
+            L = Layer()
+            L.weight = torch.randint(-63, 64, (n_out, k_in), generator=g, dtype=torch.int8).to(dev)
+            L.weight_scale = (torch.rand(n_out, 1, generator=g) / 64).to(dev)
+            w[name] = L
+        xs = {k_in: torch.randn(tokens, k_in, generator=g).to(torch.bfloat16).to(dev)
+              for _, _, k_in in shapes}
+        lin = MN.PearlLinear(True, MN.MiningConfig(), None)
+
+        def step(i):
+            lin.job = job(i)
+            for _ in range(layers):
+                for name, n_out, k_in in shapes:
+                    lin.apply_weights(w[name], xs[k_in])
+            for mnd in lin.mined:
+                MN.release_header(mnd.host_signal_header_pinned)
+            lin.mined.clear()
+        ms = _time_steps(step, args.steps, args.warmup, dev, world)
+        ops = layers * sum(2.0 * tokens * n_out * k_in for _, n_out, k_in in shapes)
+        mined = layers * len(shapes) if tokens >= 1024 else 0
+        return _line(args, world, f"config 4: Llama-3-8B linear layers x32 through PearlLinear.apply_weights "
+                     f"({tokens} tokens: {'mined' if mined else 'vanilla int8'} branch, int7 quantization "
+                     f"included)", ops, ms, {"tokens": tokens, "hidden": hidden, "mlp": mlp,
+                                             "layers": layers}, mined) if rank == 0 else None
+    if args.workload == "moe":
+        E, tokens, top_k, N, K = 8, 16384, 2, 2 * 14336, 4096
+        A = torch.randint(-64, 64, (tokens, K), generator=g, dtype=torch.int8).to(dev)
+        sa = (torch.rand(tokens, 1, generator=g) / 64).to(dev)
+        w1 = torch.randint(-64, 64, (E, N, K), generator=g, dtype=torch.int8).to(dev)
+        w1s = (torch.rand(E, N, generator=g) / 64).to(dev)
+        ids = torch.stack([torch.randperm(E, generator=g)[:top_k] for _ in range(tokens)]).to(torch.int32).to(dev)
+        out = torch.empty(tokens * top_k, N, dtype=torch.bfloat16, device=dev)
+
+        def step(i):
+            _, res = MN.moe_gemm1(A, sa, ids, w1, w1s, job(i), out=out)
+            for mnd in res.per_expert.values():
+                MN.release_header(mnd.host_signal_header_pinned)
+        ms = _time_steps(step, args.steps, args.warmup, dev, world)
+        return _line(args, world, "config 5: Mixtral-8x7B MoE GEMM1 (8 experts, 16384 tokens, top-2, "
+                     "N=2x14336, K=4096), routing + commitment + one mined GEMM per expert",
+                     2.0 * tokens * top_k * N * K, ms, {"experts": E, "tokens": tokens, "top_k": top_k,
+                                                         "n": N, "k": K}, E) if rank == 0 else None
+    raise SystemExit(f"unknown workload {args.workload}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -437,6 +549,10 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=40)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--ref-budget", type=float, default=90.0)
+    ap.add_argument("--workload", default="gemm8192",
+                    choices=["gemm8192", "gemm16384", "llama", "llama_decode", "moe"],
+                    help="gemm8192 (default) is the headline config; the others are BASELINE "
+                         "configs 3-5 measured through the miner-facing operators")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -445,7 +561,8 @@ def main():
         if args.impl == "reference":
             line = run_reference(args, world, rank)
         else:
-            line = run_ours(args, world, rank, local)
+            line = (run_ours(args, world, rank, local) if args.workload == "gemm8192"
+                    else run_workload(args, world, rank, local))
         if line is not None:
             print(json.dumps(line), flush=True)
     finally:

@@ -514,7 +514,11 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
         commit_fold(p0, p1, p2, p3);
         return;
       }
-      // ---- a tile's last chunk (fold + f32 rewrite, or fold + C) or its final C
+      // ---- a tile's last chunk (fold + f32 rewrite, or fold + C) or its final C.
+      // C goes out half by half before the release, so no more than one
+      // 32-column half is live (a spill-free kernel at 96 registers); the
+      // release comes one box store later than it could, once per slot and
+      // tile.
       float rs = 0.f;
       float2 sbv = make_float2(0.f, 0.f);
       if (do_store) {  // scales first: their latency overlaps the loads
@@ -523,8 +527,9 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
         const int c = tn * BN + 64 * wi + 2 * lane;  // this lane's two column scales
         if (c < a.N) sbv = *reinterpret_cast<const float2*>(a.sB + c);
       }
+      const int row0 = tm * BM + int(rank) * BMC + 32 * q;
+      uint8_t* box = cstage + fw * kCBoxBytes;
       uint32_t p0 = 0, p1 = 0, p2 = 0, p3 = 0;
-      uint32_t packed[32];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t v[32];
@@ -539,6 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
           tmem_st32(taddr + 32 * h, v);
         }
         if (do_store) {
+          uint32_t packed[16];
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
             const int src = 16 * h + i / 2;  // lane holding columns 32h + i, +1
@@ -546,20 +552,14 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
             const float by = __shfl_sync(0xffffffffu, sbv.y, src);
             const float f0 = is_main ? float(int(v[i])) : __uint_as_float(v[i]);
             const float f1 = is_main ? float(int(v[i + 1])) : __uint_as_float(v[i + 1]);
-            packed[16 * h + i / 2] = pack_bf16(f0 * rs * bx, f1 * rs * by);
+            packed[i / 2] = pack_bf16(f0 * rs * bx, f1 * rs * by);
           }
+          store_c_packed(a, box, packed, row0, tn * BN + 64 * wi + 32 * h, lane);
         }
       }
       if (do_convert) tmem_wait_st();
       release(do_convert);
-      if (do_fold && !commit_fold(p0, p1, p2, p3)) return;
-      if (do_store) {
-        const int row0 = tm * BM + int(rank) * BMC + 32 * q;
-        uint8_t* box = cstage + fw * kCBoxBytes;
-        const int col = tn * BN + 64 * wi;
-        store_c_packed(a, box, packed, row0, col, lane);
-        store_c_packed(a, box, packed + 16, row0, col + 32, lane);
-      }
+      if (do_fold) commit_fold(p0, p1, p2, p3);
     };
 
     uint32_t it = 0;  // operand stages issued so far, in the issuer's order
