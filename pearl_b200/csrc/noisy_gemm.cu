@@ -502,15 +502,15 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
       if (!do_convert && !do_store) {
         // ---- every chunk but a tile's last: fold only
         uint32_t p0 = 0, p1 = 0, p2 = 0, p3 = 0;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint32_t v[32];
-          __syncwarp();
-          tmem_ld32(taddr + 32 * h, v);
-          tmem_wait_ld_into(v);
-          fold32(v, p0, p1, p2, p3);
-        }
+        uint32_t v0[32], v1[32];
+        __syncwarp();
+        tmem_ld32(taddr, v0);  // both halves in flight, one wait
+        tmem_ld32(taddr + 32, v1);
+        tmem_wait_ld_into(v0);
+        tmem_wait_ld_into(v1);
         release(false);
+        fold32(v0, p0, p1, p2, p3);
+        fold32(v1, p0, p1, p2, p3);
         commit_fold(p0, p1, p2, p3);
         return;
       }
