@@ -764,6 +764,7 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
 }
 
 int denoise_convert(const int32_t* in, void* out, int64_t count, float scale, cudaStream_t s);
+int run_noising_both(const pb2_noising_params& pa, const pb2_noising_params& pb, cudaStream_t stream);
 
 }  // namespace pb2
 
@@ -774,29 +775,33 @@ extern "C" int pb2_noisy_gemm(const pb2_gemm_params* pp, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int st = set_device(p.device);
   if (st) return st;
+  pb2_noising_params qa{}, qb{};
   if (p.run_noising_a) {
     if (!p.A || !p.EAL || !p.EAR_R_major || !p.EBL_K_major) return PB2_ERR_INVALID_ARGUMENT;
-    pb2_noising_params q{};
-    q.device = p.device; q.rows = p.m; q.k = p.k; q.r = p.r;
-    q.X = p.A; q.EL = p.EAL; q.E_rmajor = p.EAR_R_major; q.E_kmajor = p.EBL_K_major;
-    q.XpE = p.ApEA;
-    q.proj = p.AxEBL_int32 ? static_cast<void*>(p.AxEBL_int32) : p.AxEBL_fp16;
-    q.proj_is_fp16 = p.AxEBL_int32 ? 0 : 1;
-    q.k_blocks_per_split = p.AxEBL_int32 ? p.k_blocks_per_split_noising_a : 0;
-    q.host_signal_sync = p.host_signal_sync;
-    if ((st = pb2_noise_A(&q, stream))) return st;
+    qa.device = p.device; qa.rows = p.m; qa.k = p.k; qa.r = p.r;
+    qa.X = p.A; qa.EL = p.EAL; qa.E_rmajor = p.EAR_R_major; qa.E_kmajor = p.EBL_K_major;
+    qa.XpE = p.ApEA;
+    qa.proj = p.AxEBL_int32 ? static_cast<void*>(p.AxEBL_int32) : p.AxEBL_fp16;
+    qa.proj_is_fp16 = p.AxEBL_int32 ? 0 : 1;
+    qa.k_blocks_per_split = p.AxEBL_int32 ? p.k_blocks_per_split_noising_a : 0;
+    qa.host_signal_sync = p.host_signal_sync;
   }
   if (p.run_noising_b) {
     if (!p.B || !p.EBR || !p.EAR_K_major || !p.EBL_R_major) return PB2_ERR_INVALID_ARGUMENT;
-    pb2_noising_params q{};
-    q.device = p.device; q.rows = p.n; q.k = p.k; q.r = p.r;
-    q.X = p.B; q.EL = p.EBR; q.E_rmajor = p.EBL_R_major; q.E_kmajor = p.EAR_K_major;
-    q.XpE = p.BpEB;
-    q.proj = p.EARxBpEB_int32 ? static_cast<void*>(p.EARxBpEB_int32) : p.EARxBpEB_fp16;
-    q.proj_is_fp16 = p.EARxBpEB_int32 ? 0 : 1;
-    q.k_blocks_per_split = p.EARxBpEB_int32 ? p.k_blocks_per_split_noising_b : 0;
-    q.host_signal_sync = p.host_signal_sync;
-    if ((st = pb2_noise_B(&q, stream))) return st;
+    qb.device = p.device; qb.rows = p.n; qb.k = p.k; qb.r = p.r;
+    qb.X = p.B; qb.EL = p.EBR; qb.E_rmajor = p.EBL_R_major; qb.E_kmajor = p.EAR_K_major;
+    qb.XpE = p.BpEB;
+    qb.proj = p.EARxBpEB_int32 ? static_cast<void*>(p.EARxBpEB_int32) : p.EARxBpEB_fp16;
+    qb.proj_is_fp16 = p.EARxBpEB_int32 ? 0 : 1;
+    qb.k_blocks_per_split = p.EARxBpEB_int32 ? p.k_blocks_per_split_noising_b : 0;
+    qb.host_signal_sync = p.host_signal_sync;
+  }
+  if (p.run_noising_a && p.run_noising_b) {
+    if ((st = run_noising_both(qa, qb, s))) return st;
+  } else if (p.run_noising_a) {
+    if ((st = pb2_noise_A(&qa, stream))) return st;
+  } else if (p.run_noising_b) {
+    if ((st = pb2_noise_B(&qb, stream))) return st;
   }
   if (!p.skip_denoising) {
     if (p.AxEBL_int32 && (st = denoise_convert(p.AxEBL_int32, p.AxEBL_fp16, p.m * p.r, 1.0f / 16384.0f, s)))

@@ -164,6 +164,21 @@ __device__ __forceinline__ void bulk_wait_all() {
 __device__ __forceinline__ void named_barrier_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
+// Named barrier that also ANDs a predicate over the participating threads:
+// every participant learns whether all of them are still on the good path,
+// so a group whose member gave up on a bounded wait leaves together.
+__device__ __forceinline__ bool named_barrier_and(int id, int count, bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %3, 0;\n\t"
+      "bar.red.and.pred q, %1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(out)
+      : "r"(id), "r"(count), "r"(uint32_t(pred))
+      : "memory");
+  return out != 0;
+}
 
 // ------------------------------------------------------------------ cluster
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -174,6 +189,13 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 // All threads of every CTA of the cluster: arrive (release) and wait (acquire).
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The two halves of cluster_sync_all, for work that needs no peer in between.
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 // Shared::cluster address of `local` in the CTA of rank `rank`.
 __device__ __forceinline__ uint32_t mapa(const void* local, uint32_t rank) {
