@@ -136,16 +136,17 @@ def run_ours(args, world, rank, local):
     hits = torch.zeros(1024, 12, dtype=torch.uint32, device=dev)
     stream = torch.cuda.current_stream(dev)
     ev_main = []
+    factors = {k: v for k, v in p.noise.items() if k not in ("EAL", "EBR")}
 
     def step(i, record=False):
         # host_signal_sync is zeroed once before the timed loop, so hit_count
         # accumulates over the steps (the header keeps the first hit).
         ka, kb = keys_a[i % n_keys], keys_b[i % n_keys]
         pg.noise_gen(R=R, key_A=ka, key_B=kb, **p.noise)
-        pg.noise_A(p.A, p.noise["EAL"], p.out["AxEBL_fp16"], p.out["ApEA"],
-                   EAR=p.noise["EAR_R_major"], EBL=p.noise["EBL_K_major"])
-        pg.noise_B(p.B, p.noise["EBR"], p.out["EARxBpEB_fp16"], p.out["BpEB"],
-                   EAR=p.noise["EAR_K_major"], EBL=p.noise["EBL_R_major"])
+        # The noising step of noisy_gemm(run_noising_A/B=True), issued apart
+        # so that the events below bracket the mined GEMM alone.
+        pg.noise_AB(p.A, p.noise["EAL"], p.out["AxEBL_fp16"], p.out["ApEA"],
+                    p.B, p.noise["EBR"], p.out["EARxBpEB_fp16"], p.out["BpEB"], **factors)
         if record:
             e0 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)

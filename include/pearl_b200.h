@@ -209,6 +209,13 @@ typedef struct pb2_noising_params {
 } pb2_noising_params;
 PB2_API int pb2_noise_A(const pb2_noising_params* p, void* stream);
 PB2_API int pb2_noise_B(const pb2_noising_params* p, void* stream);
+/* noise_A(a) and noise_B(b) of one mined GEMM, exactly as the two calls
+ * above (same outputs, same validation), in one launch when both
+ * projections are half precision with the same r and k, else as two.  No
+ * reference counterpart of its own: it is the noising step that
+ * noisy_gemm(run_noising_A, run_noising_B) performs before its GEMM
+ * (pearl_gemm_api.cpp:879-892), exposed so a caller can time it apart. */
+PB2_API int pb2_noise_AB(const pb2_noising_params* a, const pb2_noising_params* b, void* stream);
 
 /* ----------------------------------------------------- denoise_converter ---
  * Replaces denoise_converter (pearl_gemm_api.cpp:114-166): int32 -> half

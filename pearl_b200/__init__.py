@@ -32,6 +32,7 @@ from .pearl_gemm_interface import (
     kEBRScaleFactorDenoise,
     make_pow_target_tensor,
     noise_A,
+    noise_AB,
     noise_B,
     noise_gen,
     noisy_gemm,
@@ -61,6 +62,7 @@ __all__ = [
     "kEBRScaleFactorDenoise",
     "make_pow_target_tensor",
     "noise_A",
+    "noise_AB",
     "noise_B",
     "noise_gen",
     "noisy_gemm",

@@ -29,7 +29,7 @@ HIT_WORDS = 12
 
 EXPORTED = [
     "pb2_host_signal_header_size", "pb2_host_signal_sync_size", "pb2_status_string",
-    "pb2_last_cuda_error", "pb2_abi_version", "pb2_noise_gen", "pb2_noise_A", "pb2_noise_B",
+    "pb2_last_cuda_error", "pb2_abi_version", "pb2_noise_gen", "pb2_noise_A", "pb2_noise_B", "pb2_noise_AB",
     "pb2_denoise_converter", "pb2_noisy_gemm", "pb2_gemm", "pb2_inner_hash",
     "pb2_noisy_gemm_static_scratch", "pb2_tensor_hash", "pb2_required_scratchpad_bytes",
     "pb2_commitment_hash_from_merkle_roots", "pb2_build_routing_data",
@@ -127,6 +127,8 @@ def load() -> ctypes.CDLL:
                      "pb2_build_routing_data", "pb2_quantize"):
             getattr(L, name).restype = ctypes.c_int
             getattr(L, name).argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        L.pb2_noise_AB.restype = ctypes.c_int
+        L.pb2_noise_AB.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         L.pb2_inner_hash.restype = ctypes.c_int
         L.pb2_inner_hash.argtypes = [ctypes.c_int, _vp, _i64, _vp, _i64, _vp]
         L.pb2_build_routing_data_scratchpad_bytes.restype = _i64

@@ -3,20 +3,24 @@
 // Restates zk-pow/src/circuit/pearl_noise.rs (get_random_hash :46-58,
 // generate_uniform_random_matrix :61-80, generate_permutation_matrix :90-116)
 // with the reference GPU operator's output formats (noise_generation_kernel.h):
-// one keyed BLAKE3 compression per thread yields 32 random bytes, which become
-// 32 dense values (EAL / EBR, (byte & 63) - 32, plus scaled half copies) or 8
-// index pairs of a sparse factor (EAR / EBL, +1 at r0, -1 at r1), written in
-// R-major (k,r) and/or K-major (r,k) dense form.
+// one keyed BLAKE3 compression yields 32 random bytes, which become 32 dense
+// values (EAL / EBR, (byte & 63) - 32, plus scaled half copies; one
+// compression per thread) or 8 index pairs of a sparse factor (EAR / EBL, +1
+// at r0, -1 at r1; 16 compressions per block of 128 k-columns, whose threads
+// then write the block's R-major (k,r) and K-major (r,k) dense forms with
+// coalesced stores).
 #include "pb2_common.cuh"
 
 namespace pb2 {
 namespace {
 
 constexpr int kThreads = 128;
+constexpr int kSparseK = 128;  // k-columns of a sparse factor per block
 
 struct NoiseArgs {
   pb2_noise_gen_params p;
-  int64_t units_eal, units_ebr, units_ear, units_ebl, units_aux;
+  int64_t units_eal, units_ebr, units_aux;
+  int64_t blocks_eal, blocks_ebr, blocks_ear, blocks_ebl;
 };
 
 // Seed label words: "A_tensor" / "B_tensor" zero-padded to 32 bytes.
@@ -85,58 +89,84 @@ __device__ void dense_unit(const pb2_noise_gen_params& p, bool b_side, int64_t u
   }
 }
 
-__device__ void sparse_unit(const pb2_noise_gen_params& p, bool b_side, int64_t u) {
-  const int64_t k0 = u * 8;
-  if (k0 >= p.k) return;
-  uint32_t h[8];
-  random_block(b_side ? p.key_b : p.key_a, b_side, 1, uint64_t(u), h);
-  const uint32_t mask = uint32_t(p.r - 1);
-  int r0[8], r1[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    r0[j] = int(h[j] & mask);
-    r1[j] = int(uint32_t(r0[j]) ^ (1u + __umulhi(uint32_t(p.r - 1), h[j])));
-  }
-  int8_t* rmaj = b_side ? p.EBL_R_major : p.EAR_R_major;
-  int8_t* kmaj = b_side ? p.EBL_K_major : p.EAR_K_major;
+// One block per 128 k-columns of a sparse factor: 16 lanes draw the block's
+// 16 units (8 index pairs each) into shared memory, then all threads write
+// the R-major rows (k, r) and the K-major column block (r, 128) of the block
+// as coalesced 16-byte chunks.
+__device__ void sparse_block(const pb2_noise_gen_params& p, bool b_side, int64_t kb) {
+  __shared__ int16_t s_r0[kSparseK], s_r1[kSparseK];
+  const int t = threadIdx.x;
+  const int64_t kbase = kb * kSparseK;
+  const int nk = int(min(int64_t(kSparseK), p.k - kbase));  // a multiple of 16
   const int r = int(p.r);
-  if (rmaj) {
-    for (int j = 0; j < 8; ++j) {
-      const int64_t kk = k0 + j;
-      if (kk >= p.k) break;
-      uint4* row = reinterpret_cast<uint4*>(rmaj + kk * r);
-      for (int c = 0; c < r / 16; ++c) {
-        uint32_t w[4] = {0, 0, 0, 0};
-        if (r0[j] / 16 == c) w[(r0[j] % 16) / 4] |= 0x01u << (8 * (r0[j] % 4));
-        if (r1[j] / 16 == c) w[(r1[j] % 16) / 4] |= 0xFFu << (8 * (r1[j] % 4));
-        row[c] = make_uint4(w[0], w[1], w[2], w[3]);
+  if (t < kSparseK / 8) {
+    const int64_t u = kb * (kSparseK / 8) + t;
+    if (u * 8 < p.k) {
+      uint32_t h[8];
+      random_block(b_side ? p.key_b : p.key_a, b_side, 1, uint64_t(u), h);
+      const uint32_t mask = uint32_t(r - 1);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t r0 = h[j] & mask;
+        s_r0[8 * t + j] = int16_t(r0);
+        s_r1[8 * t + j] = int16_t(r0 ^ (1u + __umulhi(uint32_t(r - 1), h[j])));
       }
     }
   }
+  __syncthreads();
+  int8_t* rmaj = b_side ? p.EBL_R_major : p.EAR_R_major;
+  int8_t* kmaj = b_side ? p.EBL_K_major : p.EAR_K_major;
+  if (rmaj) {
+    // row kk: +1 at r0[kk], -1 at r1[kk] (r0 != r1)
+    const int cpr = r / 16;
+    for (int idx = t; idx < nk * cpr; idx += kThreads) {
+      const int kk = idx / cpr, c = idx % cpr;
+      const int r0 = s_r0[kk], r1 = s_r1[kk];
+      uint32_t w[4] = {0, 0, 0, 0};
+      if (r0 / 16 == c) w[(r0 % 16) / 4] |= 0x01u << (8 * (r0 % 4));
+      if (r1 / 16 == c) w[(r1 % 16) / 4] |= 0xFFu << (8 * (r1 % 4));
+      *reinterpret_cast<uint4*>(rmaj + (kbase + kk) * r + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
   if (kmaj) {
-    // Column block [k0, k0+8) of every row rr: byte j = [r0_j == rr] - [r1_j == rr].
-    for (int rr = 0; rr < r; ++rr) {
-      uint32_t lo = 0, hi = 0;
+    // row rr, column kk: [r0[kk] == rr] - [r1[kk] == rr]
+    const int cpr = nk / 16;
+    for (int idx = t; idx < r * cpr; idx += kThreads) {
+      const int rr = idx / cpr, c = idx % cpr;
+      uint32_t w[4] = {0, 0, 0, 0};
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        uint32_t b = (r0[j] == rr) ? 0x01u : ((r1[j] == rr) ? 0xFFu : 0u);
-        if (j < 4) lo |= b << (8 * j); else hi |= b << (8 * (j - 4));
+      for (int j = 0; j < 16; ++j) {
+        const int kk = 16 * c + j;
+        const uint32_t b = (s_r0[kk] == rr) ? 0x01u : ((s_r1[kk] == rr) ? 0xFFu : 0u);
+        w[j / 4] |= b << (8 * (j % 4));
       }
-      *reinterpret_cast<uint2*>(kmaj + int64_t(rr) * p.k + k0) = make_uint2(lo, hi);
+      *reinterpret_cast<uint4*>(kmaj + int64_t(rr) * p.k + kbase + 16 * c) = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
 }
 
+// Blocks are assigned whole to one part (dense EAL, dense EBR, sparse EAR,
+// sparse EBL, aux clearing), so a sparse block can synchronise.
 __global__ void __launch_bounds__(kThreads) noise_gen_kernel(const __grid_constant__ NoiseArgs a) {
-  int64_t u = int64_t(blockIdx.x) * kThreads + threadIdx.x;
-  if (u < a.units_eal) { dense_unit(a.p, false, u); return; }
-  u -= a.units_eal;
-  if (u < a.units_ebr) { dense_unit(a.p, true, u); return; }
-  u -= a.units_ebr;
-  if (u < a.units_ear) { sparse_unit(a.p, false, u); return; }
-  u -= a.units_ear;
-  if (u < a.units_ebl) { sparse_unit(a.p, true, u); return; }
-  u -= a.units_ebl;
+  int64_t b = blockIdx.x;
+  const int t = threadIdx.x;
+  if (b < a.blocks_eal) {
+    const int64_t u = b * kThreads + t;
+    if (u < a.units_eal) dense_unit(a.p, false, u);
+    return;
+  }
+  b -= a.blocks_eal;
+  if (b < a.blocks_ebr) {
+    const int64_t u = b * kThreads + t;
+    if (u < a.units_ebr) dense_unit(a.p, true, u);
+    return;
+  }
+  b -= a.blocks_ebr;
+  if (b < a.blocks_ear) { sparse_block(a.p, false, b); return; }
+  b -= a.blocks_ear;
+  if (b < a.blocks_ebl) { sparse_block(a.p, true, b); return; }
+  b -= a.blocks_ebl;
+  const int64_t u = b * kThreads + t;
   if (u < a.units_aux) {
     uint4* dst = reinterpret_cast<uint4*>(a.p.aux_buffer) + u * 2;
     int64_t words = a.p.aux_words - u * 8;
@@ -178,12 +208,14 @@ extern "C" int pb2_noise_gen(const pb2_noise_gen_params* pp, void* stream) {
   a.p = p;
   a.units_eal = (p.EAL || p.EAL_fp16) ? (p.m * p.r + 31) / 32 : 0;
   a.units_ebr = (p.EBR || p.EBR_fp16) ? (p.n * p.r + 31) / 32 : 0;
-  a.units_ear = (p.EAR_R_major || p.EAR_K_major) ? (p.k + 7) / 8 : 0;
-  a.units_ebl = (p.EBL_R_major || p.EBL_K_major) ? (p.k + 7) / 8 : 0;
   a.units_aux = p.aux_buffer ? (p.aux_words + 7) / 8 : 0;
-  const int64_t units = a.units_eal + a.units_ebr + a.units_ear + a.units_ebl + a.units_aux;
-  if (units == 0) return PB2_OK;
-  const int64_t blocks = (units + kThreads - 1) / kThreads;
+  a.blocks_eal = (a.units_eal + kThreads - 1) / kThreads;
+  a.blocks_ebr = (a.units_ebr + kThreads - 1) / kThreads;
+  a.blocks_ear = (p.EAR_R_major || p.EAR_K_major) ? (p.k + kSparseK - 1) / kSparseK : 0;
+  a.blocks_ebl = (p.EBL_R_major || p.EBL_K_major) ? (p.k + kSparseK - 1) / kSparseK : 0;
+  const int64_t blocks = a.blocks_eal + a.blocks_ebr + a.blocks_ear + a.blocks_ebl +
+                         (a.units_aux + kThreads - 1) / kThreads;
+  if (blocks == 0) return PB2_OK;
   noise_gen_kernel<<<dim3(unsigned(blocks)), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return launch_status();
 }

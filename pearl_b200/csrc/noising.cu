@@ -294,13 +294,15 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
       if (kB && lane == 0) mbar_arrive(&S.xp_ready[s]);
       // This warp's 32 x 64 block of XpE to global memory, 64 contiguous
       // bytes of a row per 4 lanes (the thread-per-row layout above would
-      // scatter the stores).
+      // scatter the stores).  The two rows of an 8-lane shared-memory
+      // wavefront are 4 apart, so their swizzled chunks use all 8 bank groups.
       {
         const int ch = 4 * c2 + (lane & 3);
+        const int sub = lane >> 2;
         const int64_t kc = int64_t(kb0 + i) * NKB + 16 * ch;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const int rr = 128 * h + 32 * q + 8 * j + (lane >> 2);
+          const int rr = 128 * h + 32 * q + 8 * j + (sub >> 1) + 4 * (sub & 1);
           const uint4 val = *reinterpret_cast<const uint4*>(xt + sw128_off(rr, ch));
           const int64_t g = int64_t(r0) + rr;
           if (g < a.rows && kc < a.K) *reinterpret_cast<uint4*>(a.XpE + g * a.K + kc) = val;
@@ -651,6 +653,11 @@ extern "C" int pb2_noise_A(const pb2_noising_params* p, void* stream) {
 extern "C" int pb2_noise_B(const pb2_noising_params* p, void* stream) {
   if (!p) return PB2_ERR_INVALID_ARGUMENT;
   return pb2::run_noising(*p, true, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int pb2_noise_AB(const pb2_noising_params* a, const pb2_noising_params* b, void* stream) {
+  if (!a || !b) return PB2_ERR_INVALID_ARGUMENT;
+  return pb2::run_noising_both(*a, *b, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int pb2_denoise_converter(const pb2_denoise_converter_params* pp, void* stream) {

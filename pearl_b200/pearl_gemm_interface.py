@@ -10,6 +10,8 @@ violation, then launches on the current torch CUDA stream through the C ABI
 
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import torch
 
@@ -192,6 +194,14 @@ def noise_gen(
 # ---------------------------------------------------------- noise_A / noise_B
 def _noising(X, EL, proj, XpE, E_rmajor, E_kmajor, rows_name, k_blocks_per_split, op,
              tile_rows, tile_k, stages):
+    p = _noising_params(X, EL, proj, XpE, E_rmajor, E_kmajor, rows_name, k_blocks_per_split, op,
+                        tile_rows, tile_k, stages)
+    with torch.cuda.device(X.device):
+        _lib.call("pb2_noise_A" if op == "noise_A" else "pb2_noise_B", p, _stream(X.device), op)
+
+
+def _noising_params(X, EL, proj, XpE, E_rmajor, E_kmajor, rows_name, k_blocks_per_split, op,
+                    tile_rows, tile_k, stages):
     rows, k = X.shape
     r = EL.shape[1]
     if k % 16 != 0:
@@ -210,8 +220,7 @@ def _noising(X, EL, proj, XpE, E_rmajor, E_kmajor, rows_name, k_blocks_per_split
         k_blocks_per_split=-1 if k_blocks_per_split is None else int(k_blocks_per_split))
     if proj.dtype == torch.float16:
         p.k_blocks_per_split = 0
-    with torch.cuda.device(X.device):
-        _lib.call("pb2_noise_A" if op == "noise_A" else "pb2_noise_B", p, _stream(X.device), op)
+    return p
 
 
 def noise_A(
@@ -242,6 +251,17 @@ def noise_A(
              tile_size_k, pipeline_stages)
 
 
+def _noise_A_checks(A, EAL, AxEBL, ApEA, EAR, EBL):
+    m, k = A.shape
+    r = EAL.shape[1]
+    _check_tensor(EAR, (k, r), torch.int8, "EAR")
+    _check_tensor(EBL, (r, k), torch.int8, "EBL")
+    _check_tensor(A, (m, k), torch.int8, "A")
+    _check_tensor(EAL, (m, r), torch.int8, "EAL")
+    _check_tensor(ApEA, (m, k), torch.int8, "ApEA")
+    _check_tensor(AxEBL, (m, r), (torch.float16, torch.int32), "AxEBL")
+
+
 def noise_B(
     B,  # n x k
     EBR,  # n x r
@@ -268,6 +288,34 @@ def noise_B(
     _check_tensor(EARxBpEB, (n, r), (torch.float16, torch.int32), "EARxBpEB")
     _noising(B, EBR, EARxBpEB, BpEB, EBL, EAR, "N", k_blocks_per_split, "noise_B", tile_size_n,
              tile_size_k, pipeline_stages)
+
+
+def noise_AB(A, EAL, AxEBL, ApEA, B, EBR, EARxBpEB, BpEB, EAR_R_major, EBL_K_major, EAR_K_major,
+             EBL_R_major, **_unused):
+    """noise_A(A, EAL, AxEBL, ApEA, EAR=EAR_R_major, EBL=EBL_K_major) and
+    noise_B(B, EBR, EARxBpEB, BpEB, EAR=EAR_K_major, EBL=EBL_R_major) of one
+    mined GEMM: the noising step that noisy_gemm(run_noising_A=True,
+    run_noising_B=True) runs before its GEMM (pearl_gemm_api.cpp:879-892),
+    as one launch when both projections are fp16.  A B200 addition with no
+    reference op of its own, so a caller can time that step apart from the
+    GEMM; the factor tensors may be passed as the noise_gen output dict."""
+    _noise_A_checks(A, EAL, AxEBL, ApEA, EAR_R_major, EBL_K_major)
+    n, k = B.shape
+    r = EBR.shape[1]
+    _check_tensor(EBL_R_major, (k, r), torch.int8, "EBL")
+    _check_tensor(EAR_K_major, (r, k), torch.int8, "EAR")
+    _check_tensor(B, (n, k), torch.int8, "B")
+    _check_tensor(EBR, (n, r), torch.int8, "EBR")
+    _check_tensor(BpEB, (n, k), torch.int8, "BpEB")
+    _check_tensor(EARxBpEB, (n, r), (torch.float16, torch.int32), "EARxBpEB")
+    pa = _noising_params(A, EAL, AxEBL, ApEA, EAR_R_major, EBL_K_major, "M", None, "noise_A",
+                         None, None, 2)
+    pb = _noising_params(B, EBR, EARxBpEB, BpEB, EBL_R_major, EAR_K_major, "N", None, "noise_B",
+                         None, None, 2)
+    with torch.cuda.device(A.device):
+        st = _lib.load().pb2_noise_AB(ctypes.byref(pa), ctypes.byref(pb),
+                                      ctypes.c_void_p(_stream(A.device)))
+        _lib.check(st, "noise_AB")
 
 
 # ------------------------------------------------------------ gemm (plain) --

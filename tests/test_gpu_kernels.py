@@ -99,6 +99,28 @@ def test_noise_B_bit_exact(n, k, r, dtype):
         assert np.array_equal(_np(proj), want)
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.int32])
+@pytest.mark.parametrize("m,n,k,r", [(1025, 384, 1024, 128), (256, 2304, 4096, 128), (512, 512, 320, 64)])
+def test_noise_AB_matches_noise_A_and_noise_B(m, n, k, r, dtype):
+    """One launch for both operands (fp16 projections) or two (int32): the
+    same bytes as the oracle's noise_A and noise_B."""
+    p = make_problem(m, n, k, r, seed=13)
+    gen_noise(p)
+    o = oracle_problem(p)
+    axebl = torch.zeros(m, r, dtype=dtype, device="cuda")
+    earx = torch.zeros(n, r, dtype=dtype, device="cuda")
+    pg.noise_AB(p.A, p.noise["EAL"], axebl, p.out["ApEA"], p.B, p.noise["EBR"], earx, p.out["BpEB"],
+                **{k_: v for k_, v in p.noise.items() if k_ not in ("EAL", "EBR")})
+    assert np.array_equal(_np(p.out["ApEA"]), o.ApEA)
+    assert np.array_equal(_np(p.out["BpEB"]), o.BpEB)
+    if dtype == torch.int32:
+        assert np.array_equal(_np(axebl), o.AxEBL)
+        assert np.array_equal(_np(earx), o.EARxBpEB)
+    else:
+        assert np.array_equal(_np(axebl), (o.AxEBL.astype(np.float32) * 2.0 ** -14).astype(np.float16))
+        assert np.array_equal(_np(earx), (o.EARxBpEB.astype(np.float32) * 2.0 ** -12).astype(np.float16))
+
+
 def test_denoise_converter_bit_exact():
     g = torch.Generator().manual_seed(4)
     a = torch.randint(-30000, 30000, (512, 128), generator=g, dtype=torch.int32)

@@ -76,6 +76,7 @@ def test_null_params_rejected():
     for name in ("pb2_noise_gen", "pb2_noise_A", "pb2_noise_B", "pb2_denoise_converter",
                  "pb2_noisy_gemm", "pb2_gemm"):
         assert getattr(L, name)(None, None) == _lib.PB2_ERR_INVALID_ARGUMENT
+    assert L.pb2_noise_AB(None, None, None) == _lib.PB2_ERR_INVALID_ARGUMENT
 
 
 def test_torch_ops_schemas_keep_reference_defaults():
