@@ -2,17 +2,20 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload: one mined int8 noisy GEMM, M = N = K = 8192,
-R = 128, seeded int7 operands, int32 accumulation, fused transcript hashing,
-keyed BLAKE3 and a difficulty check whose target yields ~1e-6 hits per hash
-tile.  One step = noise_gen + noise_A + noise_B + the mined GEMM (transcript,
-BLAKE3, target compare, denoise, bf16 C) for one GEMM; each step uses a fresh
-pair of noise seeds (another point of the nonce space).  Under torchrun every
-rank mines its own seeds (nonce-space sharding, no collective on the data
-path; weak scaling) and only hit counts are reduced after timing.
+Workload (the headline configuration): one mined int8 noisy GEMM,
+M = N = K = 8192, R = 128, seeded int7 operands, int32 accumulation, fused
+transcript hashing, keyed BLAKE3 and a difficulty check whose target yields
+~1e-6 hits per hash tile.  One step = noise_gen + the noising of both
+operands (noise_A and noise_B in one launch, as noisy_gemm(run_noising_A/B=
+True) runs it) + the mined GEMM (transcript, BLAKE3, target compare,
+denoise, bf16 C) for one GEMM; each step uses a fresh pair of noise seeds
+(another point of the nonce space).  Under torchrun every rank mines its own
+seeds (nonce-space sharding, no collective on the data path; weak scaling)
+and only hit counts are reduced after timing.
 
 metric: effective TOPS = 2*M*N*K per GEMM / time (noise and denoise work not
-counted); hashed tiles/s = M*N/128 per GEMM / time.
+counted, as in the reference's TOPS figure); hashed tiles/s = M*N/128 per
+GEMM / time.
 
 --impl reference times the reference's CPU path on the host cores: the C
 restatement in oracle/ (the Rust miner zk-pow/src/ffi/mine.rs cannot be built
@@ -38,9 +41,9 @@ M = N = K = 8192
 R = 128
 HASH_TILE = 128  # elements per protocol hash tile (2 x 64)
 TARGET_FRACTION = 1e-6  # expected hits per hash tile
-# Kernels launched per step by this implementation (noise_gen 1, noise_A 2,
-# noise_B 2, mined GEMM 1).
-LAUNCHES_PER_STEP = 6
+# Kernels of this implementation launched per step (noise_gen 1, the fused
+# noising of A and B 1, mined GEMM 1).
+LAUNCHES_PER_STEP = 3
 
 
 def target_value(frac: float) -> int:

@@ -34,7 +34,9 @@ import torch
 from blake3 import blake3
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("PEARL_REFERENCE", "/root/reference")
+REF = os.environ.get("PEARL_REFERENCE")
+if not REF:
+    sys.exit("set PEARL_REFERENCE to the reference checkout (see the module docstring)")
 sys.path.insert(0, os.path.join(REF, "miner/miner-base/src"))
 sys.path.insert(0, os.path.join(REF, "miner/miner-utils/src"))
 
