@@ -269,7 +269,10 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
         // This CTA's 128 rows of A and half of the B rows, per slot.
         const int ma = tm0 * BM + int(rank) * BMC, na = tn0 * BN + int(rank) * (BN / 2);
         const int mb = tm1 * BM + int(rank) * BMC, nb = tn1 * BN + int(rank) * (BN / 2);
-        for (int u = 0; u < units && ok; ++u) {
+        // Main units, then the denoise units, in the issuer's order.  The two
+        // loops are kept apart (and the tensor maps named, not selected), so
+        // the per-stage code on the main path stays minimal.
+        for (int u = 0; u < nmain && ok; ++u) {
           for (int s = 0; s < (two ? 2 : 1) && ok; ++s) {
             const int m0 = s ? mb : ma, n0 = s ? nb : na;
             for (int st = 0; st < stages_per_unit; ++st, ++it) {
@@ -278,17 +281,30 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
               // The leader's full barrier counts both CTAs' bytes.
               if (rank == 0) mbar_arrive_expect_tx(&S.full[j], 2 * kStageBytes);
               uint8_t* sa = stage_mem + j * kStageBytes;
-              uint8_t* sb = sa + kAStage;
-              if (u < nmain) {
-                const int kbyte = u * unit_k + st * BK;
-                tma_load_2d_2sm(&a.tmA, &S.full[j], sa, kbyte, m0);
-                tma_load_2d_2sm(&a.tmB, &S.full[j], sb, kbyte, n0);
-              } else {
-                const int d = (u - nmain) * stages_per_unit + st;
-                const bool second = d >= den_stages_per_product;
-                const int col = (d % den_stages_per_product) * (BK / 2);
-                tma_load_2d_2sm(second ? &a.tmDA1 : &a.tmDA0, &S.full[j], sa, col, m0);
-                tma_load_2d_2sm(second ? &a.tmDB1 : &a.tmDB0, &S.full[j], sb, col, n0);
+              const int kbyte = u * unit_k + st * BK;
+              tma_load_2d_2sm(&a.tmA, &S.full[j], sa, kbyte, m0);
+              tma_load_2d_2sm(&a.tmB, &S.full[j], sa + kAStage, kbyte, n0);
+            }
+          }
+        }
+        if (kDenoise) {
+          for (int d = 0; d < nden && ok; ++d) {
+            for (int s = 0; s < (two ? 2 : 1) && ok; ++s) {
+              const int m0 = s ? mb : ma, n0 = s ? nb : na;
+              for (int st = 0; st < stages_per_unit; ++st, ++it) {
+                const int j = it % kStages;
+                if (!(ok = mbar_wait(&S.empty[j], ((it / kStages) & 1) ^ 1, abort_flag, a.sync))) break;
+                if (rank == 0) mbar_arrive_expect_tx(&S.full[j], 2 * kStageBytes);
+                uint8_t* sa = stage_mem + j * kStageBytes;
+                const int ds = d * stages_per_unit + st;
+                const int col = (ds % den_stages_per_product) * (BK / 2);
+                if (ds < den_stages_per_product) {
+                  tma_load_2d_2sm(&a.tmDA0, &S.full[j], sa, col, m0);
+                  tma_load_2d_2sm(&a.tmDB0, &S.full[j], sa + kAStage, col, n0);
+                } else {
+                  tma_load_2d_2sm(&a.tmDA1, &S.full[j], sa, col, m0);
+                  tma_load_2d_2sm(&a.tmDB1, &S.full[j], sa + kAStage, col, n0);
+                }
               }
             }
           }
