@@ -175,7 +175,11 @@ __device__ void publish_hit(const MainArgs& a, int tm128, int tn, int row_in_til
   }
 }
 
-template <int BK, bool kReduce, bool kDenoise, bool kDebug>
+// kSPU = operand stages per unit (1, or 2 for R = 256): a compile-time unit
+// keeps the per-unit bookkeeping of the producer, issuer and fold warps free
+// of runtime loops and divisions (measured: several hundred cycles per unit
+// on the issuer otherwise).
+template <int BK, int kSPU, bool kReduce, bool kDenoise, bool kDebug>
 __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_constant__ MainArgs a) {
   constexpr int kAStage = BMC * BK;        // this CTA's 128 rows of A
   constexpr int kBStage = (BN / 2) * BK;   // this CTA's half of the 256 rows of B
@@ -201,12 +205,12 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
   const uint32_t rank = cluster_ctarank();  // 0 = leader (issues the MMAs), 1 = peer
   // A unit is one R-chunk of K (the transcript period) of one tile; without
   // transcript and denoise the chunk length only sets the interleaving.
-  const int unit_k = (kReduce || kDenoise) ? a.R : kTileK;
-  const int stages_per_unit = unit_k / BK;
+  constexpr int unit_k = kSPU * BK;  // = R with transcript or denoise (host-checked)
+  constexpr int stages_per_unit = kSPU;
   const int nmain = a.K / unit_k;
-  const int nden = kDenoise ? 4 : 0;  // 2 products x 2R bytes of fp16 K = 4 units of R bytes
+  constexpr int nden = kDenoise ? 4 : 0;  // 2 products x 2R bytes of fp16 K = 4 units of R bytes
   const int units = nmain + nden;
-  const int den_stages_per_product = 2 * a.R / BK;
+  constexpr int den_stages_per_product = 2 * kSPU;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
@@ -661,9 +665,9 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
 }
 
 // ------------------------------------------------------------------ host
-template <int BK, bool R_, bool D_, bool G_>
+template <int BK, int SPU, bool R_, bool D_, bool G_>
 int launch_variant(const MainArgs& a, int device, cudaStream_t s) {
-  auto kern = noisy_gemm_kernel<BK, R_, D_, G_>;
+  auto kern = noisy_gemm_kernel<BK, SPU, R_, D_, G_>;
   const int smem = stage_budget(R_) + (R_ ? kXbufBytes : 0) + kCStageBytes + int(sizeof(Smem)) + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return launch_status();
@@ -698,14 +702,14 @@ int launch_variant(const MainArgs& a, int device, cudaStream_t s) {
   return launch_status();
 }
 
-template <int BK>
-int launch_bk(const MainArgs& a, int device, bool reduce, bool denoise, bool debug, cudaStream_t s) {
-  if (reduce && denoise) return debug ? launch_variant<BK, true, true, true>(a, device, s)
-                                      : launch_variant<BK, true, true, false>(a, device, s);
-  if (reduce) return debug ? launch_variant<BK, true, false, true>(a, device, s)
-                           : launch_variant<BK, true, false, false>(a, device, s);
-  if (denoise) return launch_variant<BK, false, true, false>(a, device, s);
-  return launch_variant<BK, false, false, false>(a, device, s);
+template <int BK, int SPU>
+int launch_spu(const MainArgs& a, int device, bool reduce, bool denoise, bool debug, cudaStream_t s) {
+  if (reduce && denoise) return debug ? launch_variant<BK, SPU, true, true, true>(a, device, s)
+                                      : launch_variant<BK, SPU, true, true, false>(a, device, s);
+  if (reduce) return debug ? launch_variant<BK, SPU, true, false, true>(a, device, s)
+                           : launch_variant<BK, SPU, true, false, false>(a, device, s);
+  if (denoise) return launch_variant<BK, SPU, false, true, false>(a, device, s);
+  return launch_variant<BK, SPU, false, false, false>(a, device, s);
 }
 
 bool al16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
@@ -775,8 +779,13 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
   a.transcripts = p.transcripts;
   a.digests = p.digests;
 
-  return bk == 128 ? launch_bk<128>(a, p.device, reduce, denoise, debug, s)
-                   : launch_bk<64>(a, p.device, reduce, denoise, debug, s);
+  // Operand stages per unit: a unit is R bytes of K with transcript or
+  // denoise (R = 64: one 64-byte stage; R = 128: one; R = 256: two), else
+  // one 128-byte tile_size_k.
+  const int spu = (reduce || denoise) ? int(p.r) / bk : kTileK / bk;
+  if (bk == 64) return launch_spu<64, 1>(a, p.device, reduce, denoise, debug, s);
+  return spu == 2 ? launch_spu<128, 2>(a, p.device, reduce, denoise, debug, s)
+                  : launch_spu<128, 1>(a, p.device, reduce, denoise, debug, s);
 }
 
 int denoise_convert(const int32_t* in, void* out, int64_t count, float scale, cudaStream_t s);
