@@ -324,11 +324,13 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader only)
-    // The issuing thread's instruction stream is kept lean: the i8 and f16
-    // MMAs sit in separate loops and the accumulate flag is computed once per
-    // stage (a runtime kind switch inside the unrolled MMA block measurably
-    // slows the issue rate below the tensor pipe's).
-    if (lane == 0 && rank == 0) {
+    // The whole warp runs the issue loop and one elected lane issues each
+    // MMA and commit (the *_warp forms), so the loop state is warp-uniform.
+    // The instruction stream is kept lean: the i8 and f16 MMAs sit in
+    // separate loops and the accumulate flag is computed once per stage (a
+    // runtime kind switch inside the unrolled MMA block measurably slows the
+    // issue rate below the tensor pipe's).
+    if (rank == 0) {
       uint32_t it = 0;
       uint32_t empar = 0;  // acc_empty parity per slot
       uint32_t pend = 0;   // bit s: slot s holds a unit the fold warps have not released yet
@@ -336,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
       const uint32_t sbase = smem_u32(stage_mem);
       auto acquire = [&](int s) -> bool {
         if (!bit(pend, s)) return true;
-        if (!mbar_wait(&S.acc_empty[s], bit(empar, s), abort_flag, a.sync)) return false;
+        if (!mbar_wait_warp(&S.acc_empty[s], bit(empar, s), abort_flag, a.sync)) return false;
         empar ^= 1u << s;
         pend &= ~(1u << s);
         tc_fence_after();
@@ -344,24 +346,24 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
       };
       auto main_unit = [&](int s, int u) {
         // Operands first (usually resident already), then the slot.
-        if (!(ok = mbar_wait(&S.full[it % kStages], (it / kStages) & 1, abort_flag, a.sync))) return;
+        if (!(ok = mbar_wait_warp(&S.full[it % kStages], (it / kStages) & 1, abort_flag, a.sync))) return;
         if ((kReduce || u == 0) && !(ok = acquire(s))) return;
         const uint32_t dt = tmem + 256 * s;
         for (int st = 0; st < stages_per_unit; ++st, ++it) {
           const int j = it % kStages;
-          if (st > 0 && !(ok = mbar_wait(&S.full[j], (it / kStages) & 1, abort_flag, a.sync))) return;
+          if (st > 0 && !(ok = mbar_wait_warp(&S.full[j], (it / kStages) & 1, abort_flag, a.sync))) return;
           tc_fence_after();
           const uint64_t ad = sdesc_kmajor<BK>(sbase + j * kStageBytes);
           const uint64_t bd = sdesc_kmajor<BK>(sbase + j * kStageBytes + kAStage);
-          umma_i8_2sm(dt, ad, bd, kIdescI8, uint32_t((u | st) != 0));
+          umma_i8_2sm_warp(dt, ad, bd, kIdescI8, uint32_t((u | st) != 0));
 #pragma unroll
-          for (int ks = 1; ks < BK / 32; ++ks) umma_i8_2sm(dt, ad + 2 * ks, bd + 2 * ks, kIdescI8, 1);
-          umma_commit_2sm(&S.empty[j], kPairMask);
+          for (int ks = 1; ks < BK / 32; ++ks) umma_i8_2sm_warp(dt, ad + 2 * ks, bd + 2 * ks, kIdescI8, 1);
+          umma_commit_2sm_warp(&S.empty[j], kPairMask);
         }
         // With the transcript every unit is a fold event, and the stage's
         // commit above doubles as "accumulator ready" (one commit per unit
         // keeps the tensor pipe's queue full).  A lone event gets its own.
-        if (!kReduce && u == nmain - 1) umma_commit_2sm(&S.acc_full[s], kPairMask);
+        if (!kReduce && u == nmain - 1) umma_commit_2sm_warp(&S.acc_full[s], kPairMask);
         if (kReduce || u == nmain - 1) pend |= 1u << s;
       };
       auto denoise_unit = [&](int s, int d) {
@@ -369,16 +371,16 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
         const uint32_t dt = tmem + 256 * s;
         for (int st = 0; st < stages_per_unit; ++st, ++it) {
           const int j = it % kStages;
-          if (!(ok = mbar_wait(&S.full[j], (it / kStages) & 1, abort_flag, a.sync))) return;
+          if (!(ok = mbar_wait_warp(&S.full[j], (it / kStages) & 1, abort_flag, a.sync))) return;
           tc_fence_after();
           const uint64_t ad = sdesc_kmajor<BK>(sbase + j * kStageBytes);
           const uint64_t bd = sdesc_kmajor<BK>(sbase + j * kStageBytes + kAStage);
 #pragma unroll
-          for (int ks = 0; ks < BK / 32; ++ks) umma_f16_2sm(dt, ad + 2 * ks, bd + 2 * ks, kIdescF16, 1);
-          umma_commit_2sm(&S.empty[j], kPairMask);
+          for (int ks = 0; ks < BK / 32; ++ks) umma_f16_2sm_warp(dt, ad + 2 * ks, bd + 2 * ks, kIdescF16, 1);
+          umma_commit_2sm_warp(&S.empty[j], kPairMask);
         }
         if (d == nden - 1) {
-          umma_commit_2sm(&S.acc_full[s], kPairMask);
+          umma_commit_2sm_warp(&S.acc_full[s], kPairMask);
           pend |= 1u << s;
         }
       };
@@ -396,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
         }
       }
       // Every MMA has retired before TMEM is released.
-      umma_commit_2sm(&S.drain, 0x1);
+      umma_commit_2sm_warp(&S.drain, 0x1);
       long long t0 = clock64();
       while (!mbar_test(&S.drain, 0) && clock64() - t0 < 100000000LL) {
       }

@@ -103,6 +103,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// mbar_wait by every lane of a converged warp, with one verdict for all of
+// them (a lane that ran out of budget makes the whole warp give up).
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                               SignalSync* sync) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, sync);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // Bounded wait for warps that may idle a long time (no spin on the barrier
 // between polls, so the polling does not compete for issue slots and the
 // shared-memory pipe with latency-critical warps).
@@ -343,6 +351,41 @@ __device__ __forceinline__ void umma_commit_2sm(uint64_t* bar, uint16_t cta_mask
       "h"(cta_mask)
       : "memory");
 }
+// Warp-wide forms of the 2-SM MMA and commit: every lane of a converged warp
+// makes the call and one lane, picked by elect.sync, issues the instruction.
+// The issuing loop then runs on the whole warp, so its state (stage index,
+// descriptors, parities) is the same in every lane and the compiler can keep
+// it in the uniform datapath the tcgen05 operands are read from.
+__device__ __forceinline__ void umma_i8_2sm_warp(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred e, p;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_f16_2sm_warp(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                                  uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred e, p;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit_2sm_warp(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
+}
+
 // 2-D tiled load into this CTA's shared memory whose transaction bytes are
 // counted on the leader CTA's barrier at the same offset.
 __device__ __forceinline__ void tma_load_2d_2sm(const CUtensorMap* map, uint64_t* bar, void* dst,
