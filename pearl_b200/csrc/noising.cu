@@ -164,24 +164,30 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      tma_prefetch(&a.tmX);
-      tma_prefetch(&a.tmE1);
-      tma_prefetch(&a.tmE2);
-      mbar_arrive_expect_tx(&S.el_full, NM * R);
-      tma_load_2d(&a.tmEL, &S.el_full, el_buf, 0, r0);
+    // The whole warp walks the k-blocks; one elected lane issues the loads.
+    {
+      const bool leader = elect_one();
+      if (leader) {
+        tma_prefetch(&a.tmX);
+        tma_prefetch(&a.tmE1);
+        tma_prefetch(&a.tmE2);
+        mbar_arrive_expect_tx(&S.el_full, NM * R);
+        tma_load_2d(&a.tmEL, &S.el_full, el_buf, 0, r0);
+      }
       int i = 0;
       for (; i < nkb; ++i) {
         const int s = i % kStages;
-        if (!mbar_wait(&S.empty[s], ((i / kStages) & 1) ^ 1, abort_flag, a.sync)) break;
+        if (!mbar_wait_warp(&S.empty[s], ((i / kStages) & 1) ^ 1, abort_flag, a.sync)) break;
         uint8_t* st = stages + s * kStageSlot;
         const int k = (kb0 + i) * NKB;
-        // E first: the noise tile is computed from it while X is in flight.
-        mbar_arrive_expect_tx(&S.full_e[s], kE1Bytes + kE2Bytes);
-        tma_load_2d(&a.tmE1, &S.full_e[s], st + kXBytes, 0, k);
-        tma_load_2d(&a.tmE2, &S.full_e[s], st + kXBytes + 16384, k, 0);
-        mbar_arrive_expect_tx(&S.full_x[s], kXBytes);
-        tma_load_2d(&a.tmX, &S.full_x[s], st, k, r0);
+        if (leader) {
+          // E first: the noise tile is computed from it while X is in flight.
+          mbar_arrive_expect_tx(&S.full_e[s], kE1Bytes + kE2Bytes);
+          tma_load_2d(&a.tmE1, &S.full_e[s], st + kXBytes, 0, k);
+          tma_load_2d(&a.tmE2, &S.full_e[s], st + kXBytes + 16384, k, 0);
+          mbar_arrive_expect_tx(&S.full_x[s], kXBytes);
+          tma_load_2d(&a.tmX, &S.full_x[s], st, k, r0);
+        }
       }
       for (int j = (i > kStages ? i - kStages : 0); j < i; ++j) {
         long long t0 = clock64();
@@ -193,8 +199,10 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      bool ok = mbar_wait(&S.el_full, 0, abort_flag, a.sync);
+    // The whole warp runs the issue loop; one elected lane issues each MMA
+    // and commit (the *_warp forms).
+    {
+      bool ok = mbar_wait_warp(&S.el_full, 0, abort_flag, a.sync);
       const uint32_t el = smem_u32(el_buf);
       // projection of k-block j: D2_h += Xs_h[j] . E_kmajor[j]^T
       auto mma2 = [&](int j) {
@@ -205,7 +213,7 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
           const uint64_t ad = sdesc_kmajor<128>(st + h * (kXBytes / 2));
 #pragma unroll
           for (int ks = 0; ks < NKB / 32; ++ks)
-            umma_i8(tmem + kD2 + h * R, ad + 2 * ks, bd + 2 * ks, kIdesc2, (j | ks) != 0);
+            umma_i8_warp(tmem + kD2 + h * R, ad + 2 * ks, bd + 2 * ks, kIdesc2, (j | ks) != 0);
         }
       };
       // projection of k-block j, once its operand is in place: the original X
@@ -214,11 +222,11 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
       auto proj = [&](int j) -> bool {
         const int s = j % kStages;
         uint64_t* ready = kB ? &S.xp_ready[s] : &S.full_x[s];
-        if (!mbar_wait(ready, (j / kStages) & 1, abort_flag, a.sync)) return false;
+        if (!mbar_wait_warp(ready, (j / kStages) & 1, abort_flag, a.sync)) return false;
         tc_fence_after();
         mma2(j);
-        if (!kB) umma_commit(&S.x_free[s]);
-        umma_commit(&S.empty[s]);
+        if (!kB) umma_commit_warp(&S.x_free[s]);
+        umma_commit_warp(&S.empty[s]);
         return true;
       };
       // D1 of k-block i needs only the E tiles.  noise_B's projection of
@@ -227,8 +235,8 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
       // waits for it).
       for (int i = 0; i < nkb && ok; ++i) {
         const int s = i % kStages;
-        if (!(ok = mbar_wait(&S.full_e[s], (i / kStages) & 1, abort_flag, a.sync))) break;
-        if (i >= 1 && !(ok = mbar_wait(&S.d1_empty, (i - 1) & 1, abort_flag, a.sync))) break;
+        if (!(ok = mbar_wait_warp(&S.full_e[s], (i / kStages) & 1, abort_flag, a.sync))) break;
+        if (i >= 1 && !(ok = mbar_wait_warp(&S.d1_empty, (i - 1) & 1, abort_flag, a.sync))) break;
         tc_fence_after();
         {
           const uint64_t bd = sdesc_kmajor<R>(smem_u32(stages + s * kStageSlot + kXBytes));
@@ -237,16 +245,16 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
             const uint64_t ad = sdesc_kmajor<R>(el + h * 128 * R);  // rows 128h..
 #pragma unroll
             for (int ks = 0; ks < R / 32; ++ks)
-              umma_i8(tmem + 128 * h, ad + 2 * ks, bd + 2 * ks, kIdesc1, ks != 0);
+              umma_i8_warp(tmem + 128 * h, ad + 2 * ks, bd + 2 * ks, kIdesc1, ks != 0);
           }
-          umma_commit(&S.d1_full);
+          umma_commit_warp(&S.d1_full);
         }
         if (!kB) ok = proj(i);
         else if (i >= 1) ok = proj(i - 1);
       }
       if (ok && kB && nkb >= 1) ok = proj(nkb - 1);
-      umma_commit(&S.d2_full);
-      umma_commit(&S.drain);
+      umma_commit_warp(&S.d2_full);
+      umma_commit_warp(&S.drain);
       long long t0 = clock64();
       while (!mbar_test(&S.drain, 0) && clock64() - t0 < 100000000LL) {
       }

@@ -262,7 +262,10 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    // The whole warp walks the stage sequence; one elected lane issues the
+    // arrivals and TMA loads.
+    {
+      const bool leader = elect_one();
       uint32_t it = 0;
       bool ok = true;
       for (int t0 = first; t0 < a.num_tiles && ok; t0 += stride) {
@@ -281,13 +284,15 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
             const int m0 = s ? mb : ma, n0 = s ? nb : na;
             for (int st = 0; st < stages_per_unit; ++st, ++it) {
               const int j = it % kStages;
-              if (!(ok = mbar_wait(&S.empty[j], ((it / kStages) & 1) ^ 1, abort_flag, a.sync))) break;
-              // The leader's full barrier counts both CTAs' bytes.
-              if (rank == 0) mbar_arrive_expect_tx(&S.full[j], 2 * kStageBytes);
+              if (!(ok = mbar_wait_warp(&S.empty[j], ((it / kStages) & 1) ^ 1, abort_flag, a.sync))) break;
               uint8_t* sa = stage_mem + j * kStageBytes;
               const int kbyte = u * unit_k + st * BK;
-              tma_load_2d_2sm(&a.tmA, &S.full[j], sa, kbyte, m0);
-              tma_load_2d_2sm(&a.tmB, &S.full[j], sa + kAStage, kbyte, n0);
+              if (leader) {
+                // The leader CTA's full barrier counts both CTAs' bytes.
+                if (rank == 0) mbar_arrive_expect_tx(&S.full[j], 2 * kStageBytes);
+                tma_load_2d_2sm(&a.tmA, &S.full[j], sa, kbyte, m0);
+                tma_load_2d_2sm(&a.tmB, &S.full[j], sa + kAStage, kbyte, n0);
+              }
             }
           }
         }
@@ -297,17 +302,19 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
               const int m0 = s ? mb : ma, n0 = s ? nb : na;
               for (int st = 0; st < stages_per_unit; ++st, ++it) {
                 const int j = it % kStages;
-                if (!(ok = mbar_wait(&S.empty[j], ((it / kStages) & 1) ^ 1, abort_flag, a.sync))) break;
-                if (rank == 0) mbar_arrive_expect_tx(&S.full[j], 2 * kStageBytes);
+                if (!(ok = mbar_wait_warp(&S.empty[j], ((it / kStages) & 1) ^ 1, abort_flag, a.sync))) break;
                 uint8_t* sa = stage_mem + j * kStageBytes;
                 const int ds = d * stages_per_unit + st;
                 const int col = (ds % den_stages_per_product) * (BK / 2);
-                if (ds < den_stages_per_product) {
-                  tma_load_2d_2sm(&a.tmDA0, &S.full[j], sa, col, m0);
-                  tma_load_2d_2sm(&a.tmDB0, &S.full[j], sa + kAStage, col, n0);
-                } else {
-                  tma_load_2d_2sm(&a.tmDA1, &S.full[j], sa, col, m0);
-                  tma_load_2d_2sm(&a.tmDB1, &S.full[j], sa + kAStage, col, n0);
+                if (leader) {
+                  if (rank == 0) mbar_arrive_expect_tx(&S.full[j], 2 * kStageBytes);
+                  if (ds < den_stages_per_product) {
+                    tma_load_2d_2sm(&a.tmDA0, &S.full[j], sa, col, m0);
+                    tma_load_2d_2sm(&a.tmDB0, &S.full[j], sa + kAStage, col, n0);
+                  } else {
+                    tma_load_2d_2sm(&a.tmDA1, &S.full[j], sa, col, m0);
+                    tma_load_2d_2sm(&a.tmDB1, &S.full[j], sa + kAStage, col, n0);
+                  }
                 }
               }
             }

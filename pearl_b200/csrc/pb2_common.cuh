@@ -351,6 +351,38 @@ __device__ __forceinline__ void umma_commit_2sm(uint64_t* bar, uint16_t cta_mask
       "h"(cta_mask)
       : "memory");
 }
+// One lane of a converged warp, picked by elect.sync (call from all lanes).
+// Issue loops that run on the whole warp guard their single-thread
+// instructions (TMA, barrier arrivals) with it.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t e;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(e));
+  return e != 0;
+}
+// Warp-wide forms of the 1-SM MMA and commit (one elected lane issues).
+__device__ __forceinline__ void umma_i8_warp(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred e, p;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit_warp(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
 // Warp-wide forms of the 2-SM MMA and commit: every lane of a converged warp
 // makes the call and one lane, picked by elect.sync, issues the instruction.
 // The issuing loop then runs on the whole warp, so its state (stage index,
