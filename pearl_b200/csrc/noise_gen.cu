@@ -148,6 +148,10 @@ __device__ void sparse_block(const pb2_noise_gen_params& p, bool b_side, int64_t
 // Blocks are assigned whole to one part (dense EAL, dense EBR, sparse EAR,
 // sparse EBL, aux clearing), so a sparse block can synchronise.
 __global__ void __launch_bounds__(kThreads) noise_gen_kernel(const __grid_constant__ NoiseArgs a) {
+  // The factors are read by the previous mined GEMM in the stream: write
+  // them only once it has completed.
+  griddep_wait();
+  griddep_launch_dependents();
   int64_t b = blockIdx.x;
   const int t = threadIdx.x;
   if (b < a.blocks_eal) {
@@ -216,6 +220,15 @@ extern "C" int pb2_noise_gen(const pb2_noise_gen_params* pp, void* stream) {
   const int64_t blocks = a.blocks_eal + a.blocks_ebr + a.blocks_ear + a.blocks_ebl +
                          (a.units_aux + kThreads - 1) / kThreads;
   if (blocks == 0) return PB2_OK;
-  noise_gen_kernel<<<dim3(unsigned(blocks)), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(blocks), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see griddep_wait
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, noise_gen_kernel, a);
   return launch_status();
 }

@@ -157,6 +157,9 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Set-up above touches no global memory; it overlaps the previous kernel.
+  griddep_wait();
+  griddep_launch_dependents();
   // Peers are touched only in the projection tail: announce this CTA's
   // barriers now and wait for the peers' just before the first remote access.
   if (a.use_cluster) cluster_arrive();
@@ -461,15 +464,18 @@ int launch_noising(const NoisingArgs& a, int row_blocks, cudaStream_t s) {
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = size_t(smem);
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  unsigned nattr = 0;
+  attr[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see griddep_wait
+  attr[nattr++].val.programmaticStreamSerializationAllowed = 1;
   if (a.use_cluster) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = unsigned(a.ks);
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[nattr].id = cudaLaunchAttributeClusterDimension;
+    attr[nattr].val.clusterDim.x = 1;
+    attr[nattr].val.clusterDim.y = unsigned(a.ks);
+    attr[nattr++].val.clusterDim.z = 1;
   }
+  cfg.attrs = attr;
+  cfg.numAttrs = nattr;
   cudaLaunchKernelEx(&cfg, kern, a);
   return launch_status();
 }
@@ -592,15 +598,18 @@ int launch_noising_pair(const NoisingArgs& a, const NoisingArgs& b, int row_bloc
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = size_t(smem);
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  unsigned nattr = 0;
+  attr[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see griddep_wait
+  attr[nattr++].val.programmaticStreamSerializationAllowed = 1;
   if (a.use_cluster) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = unsigned(a.ks);
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[nattr].id = cudaLaunchAttributeClusterDimension;
+    attr[nattr].val.clusterDim.x = 1;
+    attr[nattr].val.clusterDim.y = unsigned(a.ks);
+    attr[nattr++].val.clusterDim.z = 1;
   }
+  cfg.attrs = attr;
+  cfg.numAttrs = nattr;
   cudaLaunchKernelEx(&cfg, kern, a, b);
   return launch_status();
 }

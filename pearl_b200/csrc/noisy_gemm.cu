@@ -250,6 +250,9 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
   __syncthreads();
   cluster_sync_all();  // both CTAs' barriers exist before any remote arrive or 2-SM load
   tc_fence_after();
+  // Set-up above touches no global memory; it overlaps the previous kernel.
+  griddep_wait();
+  griddep_launch_dependents();
   const uint32_t tmem = S.tmem_base;
 
   // Pair tiles are processed in rounds: round r holds tiles t0 = first + r *
@@ -707,6 +710,11 @@ int launch_variant(const MainArgs& a, int device, cudaStream_t s) {
   }
   const int pairs = std::max(1, std::min((a.num_tiles + 1) / 2, resident));
   cfg.gridDim = dim3(unsigned(2 * pairs), 1, 1);
+  cudaLaunchAttribute attrs[2] = {attr[0], {}};
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see griddep_wait
+  attrs[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 2;
   cudaLaunchKernelEx(&cfg, kern, a);
   return launch_status();
 }

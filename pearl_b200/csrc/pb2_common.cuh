@@ -168,6 +168,19 @@ __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization may start (its set-up: barriers, TMEM, shared memory) while
+// the previous kernel in the stream is still draining; griddep_wait() blocks
+// until that kernel has completed and its writes are visible (it returns at
+// once for a kernel launched without the attribute), so no global memory is
+// read or written before it.  griddep_launch_dependents() lets the next
+// kernel in the stream be scheduled early; it only starts once every CTA of
+// this grid has called it or exited.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Named barrier among `count` threads (a multiple of 32) of the CTA.
 __device__ __forceinline__ void named_barrier_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
