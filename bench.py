@@ -261,7 +261,9 @@ def run_ours(args, world, rank, local):
         },
         "clocks": clk,
     }
-    line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
+    # The CPU baseline is timed at N = 1 only: under torchrun the host cores
+    # are shared by every rank's process.
+    line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget) if world == 1 else None
     return line
 
 
