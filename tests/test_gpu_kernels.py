@@ -218,6 +218,32 @@ def test_noisy_gemm_int32_factors_and_split_k():
                                atol=ATOL, rtol=RTOL)
 
 
+def test_many_rounds_per_cta_pair_bit_exact():
+    """6144 x 6144 gives every 2-SM pair four rounds of tiles, so the
+    transcript buffers of both slots are reused (the round-alternating
+    buffers and the hash warps' clear-before-reuse); every transcript and
+    digest must still match, and an all-pass target must hit every tile
+    exactly once."""
+    m = n = 6144
+    k, r = 256, 128
+    p = make_problem(m, n, k, r, seed=61)
+    gen_noise(p)
+    o = oracle_problem(p)
+    ref = O.mine_tiles(o.ApEA, o.BpEB, r, _np(p.key_a).tobytes(), 0)
+    tiles = O.num_hash_tiles(m, n)
+    tr = torch.zeros(tiles, 16, dtype=torch.uint32, device="cuda")
+    dg = torch.zeros(tiles, 8, dtype=torch.uint32, device="cuda")
+    hits = torch.zeros(tiles + 8, 12, dtype=torch.uint32, device="cuda")
+    _, sync = run_noisy_gemm(p, 2 ** 256 - 1, transcripts=tr, digests=dg, hits=hits)
+    torch.cuda.synchronize()
+    assert np.array_equal(_np(tr), ref.transcripts)
+    assert np.array_equal(_np(dg), ref.digests)
+    f = pg.get_host_signal_sync_fields(sync)
+    assert f["error"] == 0 and f["hit_count"] == tiles
+    got = {(int(h[0]), int(h[1])) for h in _np(hits)[:tiles]}
+    assert len(got) == tiles
+
+
 def test_all_tiles_hit_and_none_hit():
     m, n, k = 256, 512, 512
     p = make_problem(m, n, k, 128, seed=5)
