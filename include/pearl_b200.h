@@ -156,6 +156,22 @@ typedef struct pb2_quant_params {
 } pb2_quant_params;
 PB2_API int pb2_quantize(const pb2_quant_params* p, void* stream);
 
+/* ---------------------------------------------------------- scatter_rows ---
+ * dst[indices[i]] = src[i] for i < rows, rows of row_bytes bytes (a multiple
+ * of 16; src, dst 16-byte aligned; indices int32).  Replaces the per-expert
+ * row scatter of the mined MoE layer, cache_flat[expert_slot_indices] =
+ * expert_output (miner/vllm-miner/src/vllm_miner/pearl_moe_experts.py:347),
+ * which torch runs as an index_put.  Indices outside [0, dst_rows) are
+ * skipped; duplicated indices leave one of their rows (unspecified which). */
+typedef struct pb2_scatter_params {
+  int device;
+  const void* src;      /* (rows, row_bytes) */
+  void* dst;            /* (dst_rows, row_bytes) */
+  const int32_t* indices; /* (rows) */
+  int64_t rows, dst_rows, row_bytes;
+} pb2_scatter_params;
+PB2_API int pb2_scatter_rows(const pb2_scatter_params* p, void* stream);
+
 /* ------------------------------------------------------------- noise_gen ---
  * Replaces noise_gen (pearl_gemm_api.cpp:168-298; kernel
  * noise_generation_kernel.h:88-758).  Any output may be NULL (not produced).

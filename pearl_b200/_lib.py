@@ -33,7 +33,7 @@ EXPORTED = [
     "pb2_denoise_converter", "pb2_noisy_gemm", "pb2_gemm", "pb2_inner_hash",
     "pb2_noisy_gemm_static_scratch", "pb2_tensor_hash", "pb2_required_scratchpad_bytes",
     "pb2_commitment_hash_from_merkle_roots", "pb2_build_routing_data",
-    "pb2_build_routing_data_scratchpad_bytes", "pb2_quantize",
+    "pb2_build_routing_data_scratchpad_bytes", "pb2_quantize", "pb2_scatter_rows",
 ]
 
 _vp = ctypes.c_void_p
@@ -104,6 +104,11 @@ class QuantParams(ctypes.Structure):
                 ("scales", _vp), ("max_val", ctypes.c_int), ("block_size", ctypes.c_int)]
 
 
+class ScatterParams(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int), ("src", _vp), ("dst", _vp), ("indices", _vp), ("rows", _i64),
+                ("dst_rows", _i64), ("row_bytes", _i64)]
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -124,7 +129,7 @@ def load() -> ctypes.CDLL:
         for name in ("pb2_noise_gen", "pb2_noise_A", "pb2_noise_B", "pb2_denoise_converter",
                      "pb2_noisy_gemm", "pb2_gemm", "pb2_noisy_gemm_static_scratch",
                      "pb2_tensor_hash", "pb2_commitment_hash_from_merkle_roots",
-                     "pb2_build_routing_data", "pb2_quantize"):
+                     "pb2_build_routing_data", "pb2_quantize", "pb2_scatter_rows"):
             getattr(L, name).restype = ctypes.c_int
             getattr(L, name).argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         L.pb2_noise_AB.restype = ctypes.c_int

@@ -27,7 +27,7 @@ import torch
 
 from . import pearl_gemm_interface as P
 from .helpers import HostSignalHeaderPinnedPool, get_host_signal_sync_fields
-from .moe import build_routing_data, get_build_routing_data_scratchpad_bytes
+from .moe import build_routing_data, get_build_routing_data_scratchpad_bytes, scatter_rows
 from .quantization import quantize
 
 MAX_VAL_7BIT = 63
@@ -373,6 +373,7 @@ def moe_gemm1(A_q, A_scales, topk_ids, w1, w1_scale, job: MiningJob,
             ctx.EBR[e * N:(e + 1) * N], ctx.EBR_fp16[e * N:(e + 1) * N], ctx.EAR_R_major,
             ctx.EBL_R_major, ctx.EAR_K_major, ctx.EBL_K_major, C_e, header, sync, ctx.pow_target,
             ctx.pow_key, config.tile_size_m, config.tile_size_n, config.tile_size_k, hits=hits)
-        out[layout.slot_indices[start:start + count].long()] = C_e
+        # out[slot_indices] = C_e (pearl_moe_experts.py:347), at HBM speed
+        scatter_rows(C_e, out, layout.slot_indices[start:start + count])
         res.per_expert[e] = MinedGemm(header, sync, ctx.commitment_hash_A, ctx.commitment_hash_B, hits)
     return out, res

@@ -64,3 +64,27 @@ def build_routing_data(
     p.scratchpad, p.scratchpad_bytes = scratchpad.data_ptr(), scratchpad.numel()
     with torch.cuda.device(topk_ids.device):
         _lib.call("pb2_build_routing_data", p, _stream(topk_ids.device), "build_routing_data")
+
+
+def scatter_rows(src: torch.Tensor, dst: torch.Tensor, indices: torch.Tensor) -> None:
+    """``dst[indices] = src`` for whole rows (2-D, contiguous, same dtype and
+    row length; ``indices`` int32 on the same device): the per-expert step
+    that puts a mined expert GEMM's rows back in routing-slot order
+    (pearl_moe_experts.py:347).  A B200 kernel in place of torch's index_put;
+    indices outside ``dst`` are skipped."""
+    if not (src.is_cuda and dst.is_cuda and indices.is_cuda):
+        _fail("scatter_rows: tensors must be on CUDA")
+    if src.dim() != 2 or dst.dim() != 2 or src.shape[1] != dst.shape[1] or src.dtype != dst.dtype:
+        _fail("scatter_rows: src and dst must be 2-D with the same row length and dtype")
+    if not (src.is_contiguous() and dst.is_contiguous() and indices.is_contiguous()):
+        _fail("scatter_rows: tensors must be contiguous")
+    if indices.dtype != torch.int32 or indices.numel() != src.shape[0]:
+        _fail("scatter_rows: indices must be int32 with one entry per src row")
+    row_bytes = src.shape[1] * src.element_size()
+    if row_bytes % 16 != 0:
+        _fail("scatter_rows: rows must be a multiple of 16 bytes")
+    p = _lib.ScatterParams(device=_device_index(src), src=src.data_ptr(), dst=dst.data_ptr(),
+                           indices=indices.data_ptr(), rows=src.shape[0], dst_rows=dst.shape[0],
+                           row_bytes=row_bytes)
+    with torch.cuda.device(src.device):
+        _lib.call("pb2_scatter_rows", p, _stream(src.device), "scatter_rows")

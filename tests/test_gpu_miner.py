@@ -225,3 +225,29 @@ def test_moe_gemm1_per_expert_parity():
         torch.testing.assert_close(got, ref.to(torch.bfloat16).float(), atol=ATOL, rtol=RTOL)
         MN.release_header(mined.host_signal_header_pinned)
     assert total > 0
+
+
+@pytest.mark.gpu
+def test_scatter_rows_matches_index_put():
+    """The MoE layer's row scatter (pb2_scatter_rows) writes exactly what
+    torch's dst[indices] = src writes, for bf16 rows of a MoE-sized width,
+    with a permutation and with indices outside dst skipped."""
+    from pearl_b200.moe import scatter_rows
+    g = torch.Generator(device="cuda").manual_seed(3)
+    rows, n = 1000, 28672
+    src = torch.randn(rows, n, generator=g, device="cuda").to(torch.bfloat16)
+    perm = torch.randperm(1500, generator=g, device="cuda")[:rows].to(torch.int32)
+    want = torch.zeros(1500, n, dtype=torch.bfloat16, device="cuda")
+    want[perm.long()] = src
+    got = torch.zeros_like(want)
+    scatter_rows(src, got, perm)
+    assert torch.equal(got, want)
+    bad = perm.clone()
+    bad[::7] = 5000  # outside dst: skipped
+    got2 = torch.zeros_like(want)
+    scatter_rows(src, got2, bad)
+    keep = torch.ones(rows, dtype=torch.bool, device="cuda")
+    keep[::7] = False
+    want2 = torch.zeros_like(want)
+    want2[perm[keep].long()] = src[keep]
+    assert torch.equal(got2, want2)
