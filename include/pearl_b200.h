@@ -87,6 +87,30 @@ PB2_API int pb2_tensor_hash(const pb2_tensor_hash_params* p, void* stream);
 /* Replaces get_required_scratchpad_bytes (tensor_hash_api.hpp:37-43). */
 PB2_API int64_t pb2_required_scratchpad_bytes(int64_t matrix_bytes, int threads_per_block);
 
+/* --------------------------------------------------------- merkle layers ---
+ * Replaces building pearl_mining.MerkleTree on the host for a hit's proof
+ * (pearl-blake3/src/merkle.rs:43-81, called by miner_base
+ * matrix_merkle_tree.py:26 and block_submission.py:25-26, zk-pow
+ * src/ffi/mine.rs:385): every layer of the keyed BLAKE3 tree over the `len`
+ * bytes at `data` zero-padded to whole 1 KiB chunks, leaves first, 32 bytes
+ * per node, layers back to back.  Layer 0 has one node per chunk; while a
+ * layer has more than two nodes the next has ceil(n / 2) (neighbours paired,
+ * an odd node carried up); a two-node layer is followed by the one-node root
+ * layer; a single chunk is its own root.  The last node is the tensor_hash of
+ * the same bytes.  `nodes` holds at least pb2_merkle_nodes(len) * 32 bytes.
+ * data 16-byte aligned; key and nodes 4-byte aligned; all on `device`. */
+typedef struct pb2_merkle_params {
+  int device;
+  const uint8_t* data;
+  int64_t len;
+  const uint8_t* key; /* 32 bytes */
+  uint8_t* nodes;
+  int64_t nodes_bytes;
+} pb2_merkle_params;
+PB2_API int pb2_merkle_layers(const pb2_merkle_params* p, void* stream);
+/* Total node count of all layers for `len` bytes (0 when len <= 0). */
+PB2_API int64_t pb2_merkle_nodes(int64_t len);
+
 /* ------------------------------------- commitment_hash_from_merkle_roots ---
  * Replaces commitment_hash_from_merkle_roots (tensor_hash_api.hpp:124-212,
  * commitment_hash_from_merkle_roots_kernel.hpp): the noise seeds

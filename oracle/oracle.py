@@ -54,6 +54,11 @@ def lib():
         L.po_commitment.argtypes = [u8p, u8p, u8p, ctypes.c_int, ctypes.c_uint32, ctypes.c_uint32,
                                     u8p, u32p, i64, u8p, u8p]
         L.po_tensor_hash.argtypes = [u8p, i64, u8p, u8p]
+        L.po_merkle_nodes.argtypes = [i64]
+        L.po_merkle_nodes.restype = i64
+        L.po_merkle_layers.argtypes = [u8p, i64, u8p, u8p]
+        L.po_chunk_cv.argtypes = [u8p, u8p, ctypes.c_uint64, u8p]
+        L.po_parent_cv.argtypes = [u8p, u8p, u8p, ctypes.c_int, u8p]
         L.po_num_threads.restype = ctypes.c_int
         L.po_set_num_threads.argtypes = [ctypes.c_int]
         _lib = L
@@ -237,6 +242,112 @@ def tensor_hash(data: np.ndarray, key: bytes) -> bytes:
     lib().po_tensor_hash(_p(d, ctypes.c_uint8) if d.size else None, d.size,
                          _p(_bytes32(key), ctypes.c_uint8), _p(out, ctypes.c_uint8))
     return out.tobytes()
+
+
+# ----------------------------------------------------------------- merkle ---
+def merkle_layers(data: np.ndarray, key: bytes) -> list[np.ndarray]:
+    """Layers (leaves first) of the BLAKE3 Merkle tree over the bytes
+    zero-padded to 1 KiB chunks (pearl-blake3/src/merkle.rs:43-81 on
+    pad_to_chunk_boundary, :15-27); each layer is an (n, 32) uint8 array."""
+    d = np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+    total = int(lib().po_merkle_nodes(d.size))
+    nodes = np.zeros((max(total, 1), 32), np.uint8)
+    if d.size:
+        lib().po_merkle_layers(_p(d, ctypes.c_uint8), d.size, _p(_bytes32(key), ctypes.c_uint8),
+                               _p(nodes, ctypes.c_uint8))
+    sizes, n = [], (d.size + 1023) // 1024
+    if n:
+        sizes.append(n)
+        while n > 2:
+            n = (n + 1) // 2
+            sizes.append(n)
+        if n == 2:
+            sizes.append(1)
+    out, off = [], 0
+    for s in sizes:
+        out.append(nodes[off:off + s])
+        off += s
+    return out
+
+
+def multileaf_proof(layers: list[np.ndarray], padded: bytes, leaf_indices) -> dict:
+    """MerkleTree::get_multileaf_proof (pearl-blake3/src/merkle.rs:104-155):
+    sorted unique leaves, their 1 KiB chunks, and the sibling CVs in the
+    order the level walk meets them."""
+    unique = sorted(set(int(i) for i in leaf_indices))
+    total = len(layers[0])
+    assert unique and unique[-1] < total
+    leaf_data = [bytes(padded[i * 1024:(i + 1) * 1024]).ljust(1024, b"\0") for i in unique]
+    siblings, cur, level_len, level = [], unique, total, 0
+    while level_len > 1 and cur:
+        nodes, cs = layers[level], set(cur)
+        for i in cur:
+            if i % 2 == 1:
+                if i - 1 not in cs:
+                    siblings.append(nodes[i - 1].tobytes())
+            elif i + 1 not in cs and i + 1 < level_len:
+                siblings.append(nodes[i + 1].tobytes())
+        cur = sorted(set(i // 2 for i in cur))
+        level_len = (level_len + 1) // 2
+        level += 1
+    return {"leaf_data": leaf_data, "leaf_indices": unique, "total_leaves": total,
+            "root": layers[-1][0].tobytes(), "siblings": siblings}
+
+
+def chunk_cv(key: bytes, chunk: bytes, index: int) -> bytes:
+    c = np.frombuffer(bytes(chunk), np.uint8).copy()
+    assert c.size == 1024
+    out = np.zeros(32, np.uint8)
+    lib().po_chunk_cv(_p(_bytes32(key), ctypes.c_uint8), _p(c, ctypes.c_uint8), index,
+                      _p(out, ctypes.c_uint8))
+    return out.tobytes()
+
+
+def parent_cv(key: bytes, left: bytes, right: bytes, root: bool) -> bytes:
+    l_, r_ = _bytes32(left), _bytes32(right)
+    out = np.zeros(32, np.uint8)
+    lib().po_parent_cv(_p(_bytes32(key), ctypes.c_uint8), _p(l_, ctypes.c_uint8),
+                       _p(r_, ctypes.c_uint8), int(root), _p(out, ctypes.c_uint8))
+    return out.tobytes()
+
+
+def proof_root(proof: dict, key: bytes):
+    """MerkleProof::compute_root (pearl-blake3/src/merkle.rs:222-289): the
+    root rebuilt from the leaf chunks and the siblings, None when the proof
+    has the wrong shape."""
+    idx = proof["leaf_indices"]
+    if not idx:
+        return None
+    cur = {i: chunk_cv(key, d, i) for i, d in zip(idx, proof["leaf_data"])}
+    level_len = proof["total_leaves"]
+    if level_len == 1:
+        if proof["siblings"]:
+            return None
+        # the single leaf is the root: the keyed hash of its chunk
+        return blake3(proof["leaf_data"][0], key)
+    sib = iter(proof["siblings"])
+    try:
+        while level_len > 2:
+            nxt = {}
+            for i in sorted(cur):
+                cv = cur[i]
+                if i % 2 == 0:
+                    if i + 1 in cur:
+                        nxt[i // 2] = parent_cv(key, cv, cur[i + 1], False)
+                    elif i + 1 < level_len:
+                        nxt[i // 2] = parent_cv(key, cv, next(sib), False)
+                    else:
+                        nxt[i // 2] = cv
+                elif i - 1 not in cur:
+                    nxt[i // 2] = parent_cv(key, next(sib), cv, False)
+            cur, level_len = nxt, (level_len + 1) // 2
+        left = cur[0] if 0 in cur else next(sib)
+        right = cur[1] if 1 in cur else next(sib)
+    except StopIteration:
+        return None
+    if next(sib, None) is not None:
+        return None
+    return parent_cv(key, left, right, True)
 
 
 # ---------------------------------------------------------------- routing ---

@@ -492,6 +492,81 @@ PO_EXPORT void po_tensor_hash(const uint8_t* data, int64_t len,
   free(buf);
 }
 
+/* ------------------------------------------------------------------------- */
+/* Merkle tree of a zero-padded tensor: pearl-blake3/src/merkle.rs:43-81      */
+/* ------------------------------------------------------------------------- */
+
+static void load_key(const uint8_t key32[32], uint32_t key[8]) {
+  for (int i = 0; i < 8; ++i) key[i] = load_le32(key32 + 4 * i);
+}
+
+/* Number of nodes over all layers for `len` bytes padded to whole chunks:
+ * layer 0 holds one CV per chunk; while a layer has more than two nodes the
+ * next one has ceil(n / 2); a two-node layer is followed by the root. */
+PO_EXPORT int64_t po_merkle_nodes(int64_t len) {
+  int64_t n = (len + 1023) / 1024;
+  if (n <= 1) return n;
+  int64_t total = n;
+  while (n > 2) {
+    n = (n + 1) / 2;
+    total += n;
+  }
+  return total + 1;
+}
+
+/* CV of 1 KiB chunk `index` (a leaf, never the root). */
+PO_EXPORT void po_chunk_cv(const uint8_t key32[32], const uint8_t chunk[1024], uint64_t index,
+                           uint8_t out[32]) {
+  uint32_t key[8], cv[8];
+  load_key(key32, key);
+  b3_chunk_cv(key, B3_KEYED_HASH, chunk, 1024, index, 0, cv);
+  for (int i = 0; i < 8; ++i) store_le32(out + 4 * i, cv[i]);
+}
+
+/* Parent CV of two child CVs; `root` adds the ROOT flag (hasher.rs root_cv). */
+PO_EXPORT void po_parent_cv(const uint8_t key32[32], const uint8_t left[32], const uint8_t right[32],
+                            int root, uint8_t out[32]) {
+  uint32_t key[8], l[8], r[8], cv[8];
+  load_key(key32, key);
+  for (int i = 0; i < 8; ++i) {
+    l[i] = load_le32(left + 4 * i);
+    r[i] = load_le32(right + 4 * i);
+  }
+  b3_parent_cv(key, B3_KEYED_HASH, l, r, root, cv);
+  for (int i = 0; i < 8; ++i) store_le32(out + 4 * i, cv[i]);
+}
+
+/* All layers, leaves first, 32 bytes per node (po_merkle_nodes(len) nodes).
+ * One chunk: the single node is the keyed hash of the padded chunk. */
+PO_EXPORT void po_merkle_layers(const uint8_t* data, int64_t len, const uint8_t key32[32],
+                                uint8_t* nodes) {
+  int64_t n = (len + 1023) / 1024;
+  if (n == 0) return;
+  uint32_t key[8];
+  load_key(key32, key);
+  uint8_t chunk[1024];
+  for (int64_t c = 0; c < n; ++c) {
+    int64_t off = c * 1024, take = len - off < 1024 ? len - off : 1024;
+    memset(chunk, 0, sizeof(chunk));
+    memcpy(chunk, data + off, (size_t)take);
+    uint32_t cv[8];
+    b3_chunk_cv(key, B3_KEYED_HASH, chunk, 1024, (uint64_t)c, n == 1, cv);
+    for (int i = 0; i < 8; ++i) store_le32(nodes + 32 * c + 4 * i, cv[i]);
+  }
+  uint8_t* prev = nodes;
+  int64_t cnt = n;
+  while (cnt > 1) {
+    uint8_t* next = prev + 32 * cnt;
+    const int root = cnt == 2;
+    int64_t pairs = cnt / 2;
+    for (int64_t i = 0; i < pairs; ++i)
+      po_parent_cv(key32, prev + 64 * i, prev + 64 * i + 32, root, next + 32 * i);
+    if (cnt & 1) memcpy(next + 32 * pairs, prev + 32 * (cnt - 1), 32);
+    prev = next;
+    cnt = pairs + (cnt & 1);
+  }
+}
+
 PO_EXPORT int po_num_threads(void) {
 #ifdef _OPENMP
   return omp_get_max_threads();

@@ -34,6 +34,7 @@ EXPORTED = [
     "pb2_noisy_gemm_static_scratch", "pb2_tensor_hash", "pb2_required_scratchpad_bytes",
     "pb2_commitment_hash_from_merkle_roots", "pb2_build_routing_data",
     "pb2_build_routing_data_scratchpad_bytes", "pb2_quantize", "pb2_scatter_rows",
+    "pb2_merkle_layers", "pb2_merkle_nodes",
 ]
 
 _vp = ctypes.c_void_p
@@ -104,6 +105,11 @@ class QuantParams(ctypes.Structure):
                 ("scales", _vp), ("max_val", ctypes.c_int), ("block_size", ctypes.c_int)]
 
 
+class MerkleParams(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int), ("data", _vp), ("len", _i64), ("key", _vp), ("nodes", _vp),
+                ("nodes_bytes", _i64)]
+
+
 class ScatterParams(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int), ("src", _vp), ("dst", _vp), ("indices", _vp), ("rows", _i64),
                 ("dst_rows", _i64), ("row_bytes", _i64)]
@@ -129,7 +135,7 @@ def load() -> ctypes.CDLL:
         for name in ("pb2_noise_gen", "pb2_noise_A", "pb2_noise_B", "pb2_denoise_converter",
                      "pb2_noisy_gemm", "pb2_gemm", "pb2_noisy_gemm_static_scratch",
                      "pb2_tensor_hash", "pb2_commitment_hash_from_merkle_roots",
-                     "pb2_build_routing_data", "pb2_quantize", "pb2_scatter_rows"):
+                     "pb2_build_routing_data", "pb2_quantize", "pb2_scatter_rows", "pb2_merkle_layers"):
             getattr(L, name).restype = ctypes.c_int
             getattr(L, name).argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         L.pb2_noise_AB.restype = ctypes.c_int
@@ -138,6 +144,8 @@ def load() -> ctypes.CDLL:
         L.pb2_inner_hash.argtypes = [ctypes.c_int, _vp, _i64, _vp, _i64, _vp]
         L.pb2_build_routing_data_scratchpad_bytes.restype = _i64
         L.pb2_build_routing_data_scratchpad_bytes.argtypes = [_i64]
+        L.pb2_merkle_nodes.restype = _i64
+        L.pb2_merkle_nodes.argtypes = [_i64]
         L.pb2_required_scratchpad_bytes.restype = _i64
         L.pb2_required_scratchpad_bytes.argtypes = [_i64, ctypes.c_int]
         L.pb2_host_signal_header_size.restype = _i64

@@ -181,6 +181,88 @@ __global__ void __launch_bounds__(1024) root_fold_kernel(const TensorHashArgs a)
   if (t < 8) a.out[t] = nodes[t];
 }
 
+// ------------------------------------------------------------ merkle layers
+// Every layer of the tree tensor_hash folds, kept for a proof of a hit's rows
+// (pearl-blake3/src/merkle.rs:43-81 over the zero-padded tensor): layer 0
+// holds one CV per chunk; while a layer has more than two nodes the next one
+// pairs neighbours (an odd node carried up unchanged); a two-node layer is
+// followed by the root (ROOT flag).  A single chunk is its own root.  One
+// 128-thread CTA per group of 128 aligned chunks writes layers 0-7 of its
+// group (all of them when the group is the whole tree); one CTA then builds
+// the layers above 7 from the group nodes.
+constexpr int kMerkleGroup = 128;
+constexpr int kMerkleGroupLevels = 7;  // log2(kMerkleGroup)
+constexpr int kMerkleMaxLayers = 64;
+
+struct MerkleArgs {
+  TensorHashArgs h;  // data, len, chunks, num_groups (of kMerkleGroup chunks), key
+  uint32_t* nodes;   // 8 words per node, layers back to back
+  uint64_t off[kMerkleMaxLayers];
+  int layers;
+};
+
+__global__ void __launch_bounds__(kMerkleGroup) merkle_group_kernel(const MerkleArgs a) {
+  __shared__ uint32_t cvs[kMerkleGroup][9];
+  __shared__ uint32_t key[8];
+  const int t = threadIdx.x;
+  const uint64_t first = uint64_t(blockIdx.x) * kMerkleGroup;
+  const int n = int(a.h.chunks - first < uint64_t(kMerkleGroup) ? a.h.chunks - first : uint64_t(kMerkleGroup));
+  const bool single = a.h.num_groups == 1;
+  if (t < 8) key[t] = a.h.key[t];
+  __syncthreads();
+  if (t < n) {
+    uint32_t cv[8];
+    chunk_cv(a.h, key, first + t, a.h.chunks == 1, cv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      cvs[t][i] = cv[i];
+      a.nodes[(a.off[0] + first + t) * 8 + i] = cv[i];
+    }
+  }
+  __syncthreads();
+  // A group that is the whole tree folds to the root; otherwise every group
+  // folds to its layer-7 node, a short last group carrying its last node up.
+  const int top = single ? a.layers - 1 : kMerkleGroupLevels;
+  int cnt = n;
+  for (int l = 1; l <= top; ++l) {
+    const int pairs = cnt / 2;
+    uint32_t out[8];
+    if (t < pairs) parent_cv(key, cvs[2 * t], cvs[2 * t + 1], single && cnt == 2, out);
+    __syncthreads();
+    if (t < pairs) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) cvs[t][i] = out[i];
+    }
+    if ((cnt & 1) && t < 8) cvs[pairs][t] = cvs[cnt - 1][t];
+    __syncthreads();
+    cnt = pairs + (cnt & 1);
+    uint32_t* dst = a.nodes + (a.off[l] + (first >> l)) * 8;
+    for (int e = t; e < cnt * 8; e += kMerkleGroup) dst[e] = cvs[e >> 3][e & 7];
+  }
+}
+
+__global__ void __launch_bounds__(1024) merkle_top_kernel(const MerkleArgs a) {
+  __shared__ uint32_t key[8];
+  const uint32_t t = threadIdx.x;
+  if (t < 8) key[t] = a.h.key[t];
+  __syncthreads();
+  uint64_t cnt = a.h.num_groups;
+  for (int l = kMerkleGroupLevels + 1; l < a.layers; ++l) {
+    const uint32_t* prev = a.nodes + a.off[l - 1] * 8;
+    uint32_t* next = a.nodes + a.off[l] * 8;
+    const uint64_t pairs = cnt / 2;
+    for (uint64_t i = t; i < pairs; i += blockDim.x) {
+      uint32_t out[8];
+      parent_cv(key, prev + 16 * i, prev + 16 * i + 8, cnt == 2, out);
+#pragma unroll
+      for (int w = 0; w < 8; ++w) next[8 * i + w] = out[w];
+    }
+    if ((cnt & 1) && t < 8) next[8 * pairs + t] = prev[8 * (cnt - 1) + t];
+    __syncthreads();
+    cnt = pairs + (cnt & 1);
+  }
+}
+
 // ---------------------------------------------------------------- commitment
 struct CommitArgs {
   const uint32_t* root_a;
@@ -318,6 +400,66 @@ extern "C" int pb2_tensor_hash(const pb2_tensor_hash_params* pp, void* stream) {
   if ((st = launch_status())) return st;
   if (a.num_groups > 1) {
     root_fold_kernel<<<1, 1024, 0, s>>>(a);
+    if ((st = launch_status())) return st;
+  }
+  return PB2_OK;
+}
+
+// Layer sizes of the tree over `len` bytes; returns the layer count (0 when
+// len <= 0 or more than kMerkleMaxLayers) and the total node count.
+static int merkle_layout(int64_t len, uint64_t* off, int64_t* total) {
+  *total = 0;
+  if (len <= 0) return 0;
+  uint64_t n = (uint64_t(len) + pb2::kChunkBytes - 1) / pb2::kChunkBytes;
+  int layers = 0;
+  uint64_t at = 0;
+  for (;;) {
+    if (layers == pb2::kMerkleMaxLayers) return 0;
+    if (off) off[layers] = at;
+    ++layers;
+    at += n;
+    if (n <= 1) break;
+    n = n == 2 ? 1 : (n + 1) / 2;
+  }
+  *total = int64_t(at);
+  return layers;
+}
+
+extern "C" int64_t pb2_merkle_nodes(int64_t len) {
+  int64_t total;
+  merkle_layout(len, nullptr, &total);
+  return total;
+}
+
+extern "C" int pb2_merkle_layers(const pb2_merkle_params* pp, void* stream) {
+  using namespace pb2;
+  if (!pp) return PB2_ERR_INVALID_ARGUMENT;
+  const pb2_merkle_params& p = *pp;
+  if (p.len <= 0 || !p.data || !p.key || !p.nodes) return PB2_ERR_INVALID_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(p.data) % 16 != 0 || !al4(p.key) || !al4(p.nodes))
+    return PB2_ERR_INVALID_ARGUMENT;
+  MerkleArgs a;
+  int64_t total;
+  a.layers = merkle_layout(p.len, a.off, &total);
+  if (a.layers == 0 || p.nodes_bytes < total * 32) return PB2_ERR_INVALID_ARGUMENT;
+  const uint64_t chunks = (uint64_t(p.len) + kChunkBytes - 1) / kChunkBytes;
+  const uint64_t groups = (chunks + kMerkleGroup - 1) / kMerkleGroup;
+  if (groups > INT32_MAX) return PB2_ERR_INVALID_ARGUMENT;
+  int st = set_device(p.device);
+  if (st) return st;
+  a.h.data = p.data;
+  a.h.len = uint64_t(p.len);
+  a.h.chunks = chunks;
+  a.h.num_groups = uint32_t(groups);
+  a.h.key = reinterpret_cast<const uint32_t*>(p.key);
+  a.h.roots = nullptr;
+  a.h.out = nullptr;
+  a.nodes = reinterpret_cast<uint32_t*>(p.nodes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  merkle_group_kernel<<<unsigned(groups), kMerkleGroup, 0, s>>>(a);
+  if ((st = launch_status())) return st;
+  if (groups > 1) {
+    merkle_top_kernel<<<1, 1024, 0, s>>>(a);
     if ((st = launch_status())) return st;
   }
   return PB2_OK;

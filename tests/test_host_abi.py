@@ -59,7 +59,7 @@ def _c_sizeof(struct: str) -> int:
     ("pb2_denoise_converter_params", "DenoiseConverterParams"), ("pb2_gemm_params", "GemmParams"),
     ("pb2_tensor_hash_params", "TensorHashParams"), ("pb2_commitment_params", "CommitmentParams"),
     ("pb2_routing_params", "RoutingParams"), ("pb2_quant_params", "QuantParams"),
-    ("pb2_scatter_params", "ScatterParams")])
+    ("pb2_scatter_params", "ScatterParams"), ("pb2_merkle_params", "MerkleParams")])
 def test_param_struct_layout_matches_header(cname, pyname):
     assert _c_sizeof(cname) == ctypes.sizeof(getattr(_lib, pyname))
 
