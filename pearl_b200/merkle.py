@@ -229,3 +229,37 @@ def open_rows(tensor: torch.Tensor, key: bytes, row_indices) -> MerkleProof:
     proof of the chunks holding ``row_indices`` of ``tensor``."""
     tree = MatrixMerkleTree(tensor, key)
     return tree.get_multileaf_proof(tree.leaf_indices_from_rows(row_indices))
+
+
+@dataclass
+class MoERoutingProof:
+    """The routing part of a MoE proof (block_submission.py:64-88,
+    MoEProofParams): which expert's segment of the routed token list the hit
+    used, and the Merkle proof of the opened routing entries."""
+    e: int
+    top_k: int
+    expert_idx: int
+    routing_end_offsets: list[int]
+    inner_a_rows: list[int]
+    routing_proof: MerkleProof
+
+
+def moe_routing_proof(routing_data: torch.Tensor, routing_end_offsets, expert_idx: int, inner_a_rows,
+                      key: bytes, num_experts: int, top_k: int) -> MoERoutingProof:
+    """_build_moe_proof_params (block_submission.py:64-88) on the GPU copy of
+    the routing data: each u32 entry of ``routing_data`` (the expert-sorted
+    token list of build_routing_data) is one 4-byte row of the committed
+    matrix; the expert's segment starts at the previous expert's exclusive
+    end; the opened rows are that start plus the hit's rows inside the
+    expert's A slice."""
+    if routing_data.dtype not in (torch.int32, torch.uint32):
+        raise ValueError("routing_data must be a 32-bit tensor")
+    offsets = [int(x) for x in routing_end_offsets]
+    if not 0 <= expert_idx < len(offsets):
+        raise ValueError("expert_idx out of range")
+    rows = routing_data.contiguous().view(torch.int8).reshape(-1, 4)
+    tree = MatrixMerkleTree(rows, key)
+    start = 0 if expert_idx == 0 else offsets[expert_idx - 1]
+    global_rows = [start + int(r) for r in inner_a_rows]
+    proof = tree.get_multileaf_proof(tree.leaf_indices_from_rows(global_rows))
+    return MoERoutingProof(num_experts, top_k, expert_idx, offsets, [int(r) for r in inner_a_rows], proof)

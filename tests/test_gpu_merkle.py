@@ -63,3 +63,34 @@ def test_matrix_tree_leaves():
     a = MK.MatrixMerkleTree(t1.cuda(), KEY).leaf_hashes
     b = MK.MatrixMerkleTree(t2.cuda(), KEY).leaf_hashes
     assert len(a) == 2 and a[0] != b[0] and a[1] == b[1]
+
+
+def test_moe_routing_proof():
+    """The routing proof of a hit in expert 3's slice: the opened chunks hold
+    the routed tokens at the global rows, and the proof rebuilds the root of
+    the routing data's tree (the routing_root of the MoE commitment)."""
+    from pearl_b200 import moe
+    g = torch.Generator().manual_seed(4)
+    tokens, top_k, E = 3000, 2, 8
+    ids = torch.stack([torch.randperm(E, generator=g)[:top_k] for _ in range(tokens)]).to(torch.int32).cuda()
+    n = tokens * top_k
+    rd = torch.empty(n, dtype=torch.int32, device="cuda")
+    si = torch.empty(n, dtype=torch.int32, device="cuda")
+    off = torch.empty(E, dtype=torch.int32, device="cuda")
+    scratch = torch.empty(moe.get_build_routing_data_scratchpad_bytes(n), dtype=torch.uint8, device="cuda")
+    moe.build_routing_data(ids, rd, si, off, scratch, E)
+    offs = off.tolist()
+    inner = [0, 8, 300, offs[3] - offs[2] - 1]
+    res = MK.moe_routing_proof(rd, offs, 3, inner, KEY, E, top_k)
+    p = res.routing_proof
+    pr = {"leaf_data": p.leaf_data, "leaf_indices": p.leaf_indices, "total_leaves": p.total_leaves,
+          "root": p.root, "siblings": p.siblings}
+    assert p.root == O.tensor_hash(rd.cpu().numpy(), KEY)
+    assert O.proof_root(pr, KEY) == p.root
+    data = {i: d for i, d in zip(p.leaf_indices, p.leaf_data)}
+    host = rd.cpu().numpy()
+    for r in inner:
+        gr = offs[2] + r
+        leaf, at = divmod(4 * gr, 1024)
+        assert np.frombuffer(data[leaf][at:at + 4], np.int32)[0] == host[gr]
+    assert (res.e, res.top_k, res.expert_idx, res.inner_a_rows) == (E, top_k, 3, inner)
