@@ -21,6 +21,7 @@ the commitment hashes of every mined GEMM (``MinedGemm``)."""
 
 from __future__ import annotations
 
+from collections import OrderedDict
 from dataclasses import dataclass, field
 
 import torch
@@ -101,6 +102,28 @@ def _u8(b: bytes, device) -> torch.Tensor:
     return torch.frombuffer(bytearray(b), dtype=torch.uint8).to(device)
 
 
+_JOB_TENSORS: "OrderedDict[tuple, tuple[torch.Tensor, torch.Tensor]]" = OrderedDict()
+
+
+def _job_tensors(job: MiningJob, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """The job's commitment key and pow target as device tensors, made once
+    per (job, device): a copy from pageable host memory waits for the
+    stream, and every mined GEMM of a job reads the same two values.  The
+    cached tensors are never written."""
+    dev = torch.device(device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    k = (job.hash_key, job.pow_target, idx)
+    hit = _JOB_TENSORS.get(k)
+    if hit is None:
+        hit = (_u8(job.hash_key, dev), P.make_pow_target_tensor(job.pow_target, dev))
+        _JOB_TENSORS[k] = hit
+        while len(_JOB_TENSORS) > 64:
+            _JOB_TENSORS.popitem(last=False)
+    else:
+        _JOB_TENSORS.move_to_end(k)
+    return hit
+
+
 # ------------------------------------------------------------ quantization --
 def quant_7bit(x, smooth_scale=None, block_size: int = NO_HADAMARD_BLOCK_SIZE):
     return _quant(x, MAX_VAL_7BIT, smooth_scale, block_size)
@@ -154,22 +177,55 @@ def _tensor_root(data_u8: torch.Tensor, key: torch.Tensor, scratch: torch.Tensor
     return out
 
 
+_SIDE_STREAMS: dict[int, torch.cuda.Stream] = {}
+
+
+def _side_stream(device: torch.device) -> torch.cuda.Stream:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    s = _SIDE_STREAMS.get(idx)
+    if s is None:
+        s = _SIDE_STREAMS[idx] = torch.cuda.Stream(device)
+    return s
+
+
+def _tensor_root_async(data_u8: torch.Tensor, key: torch.Tensor):
+    """The tensor_hash root of ``data_u8`` computed on a side stream, so that
+    it overlaps the caller's next kernels (the other operand's hash, the
+    activation quantization).  Returns (root, event); the caller's stream
+    waits on the event before it reads root."""
+    main = torch.cuda.current_stream(data_u8.device)
+    side = _side_stream(data_u8.device)
+    side.wait_stream(main)  # the data and the key are ready
+    with torch.cuda.stream(side):
+        root = _tensor_root(data_u8, key)
+    data_u8.record_stream(side)
+    key.record_stream(side)
+    root.record_stream(main)
+    done = torch.cuda.Event()
+    done.record(side)
+    return root, done
+
+
 def pearl_gemm_noisy(a, b, scale_a, scale_b, out_dtype, job: MiningJob,
-                     config: MiningConfig = MiningConfig(), *, hits: torch.Tensor | None = None):
+                     config: MiningConfig = MiningConfig(), *, hits: torch.Tensor | None = None,
+                     b_root=None):
     """Mined C = A . B^T (gemm_operators.py:68-264): commitment to A and B,
     seeded noise, noisy GEMM with the fused transcript / BLAKE3 / target
-    check, denoised bf16 output.  Returns (C, MinedGemm)."""
+    check, denoised bf16 output.  Returns (C, MinedGemm).  B's root is
+    hashed on a side stream beside A's, or taken from ``b_root`` (the
+    (root, event) of an earlier _tensor_root_async of the same B and key)."""
     assert out_dtype is torch.bfloat16 or out_dtype is torch.float16
     m, k = a.shape
     n = b.shape[0]
     r = config.noise_rank
     device = a.device
     C = torch.empty((m, n), dtype=out_dtype, device=device)
-    scratch = torch.empty(P.get_required_scratchpad_bytes(max(m * k, n * k)), dtype=torch.uint8,
-                          device=device)
-    key_tensor = _u8(job.hash_key, device)
-    A_root = _tensor_root(a.view(torch.uint8), key_tensor, scratch)
-    B_root = _tensor_root(b.view(torch.uint8), key_tensor, scratch)
+    key_tensor, target_tensor = _job_tensors(job, device)
+    if b_root is None:
+        b_root = _tensor_root_async(b.view(torch.uint8), key_tensor)
+    A_root = _tensor_root(a.view(torch.uint8), key_tensor)
+    B_root, b_ready = b_root
+    torch.cuda.current_stream(device).wait_event(b_ready)
     ch_A = torch.empty(32, device=device, dtype=torch.uint8)
     ch_B = torch.empty(32, device=device, dtype=torch.uint8)
     P.commitment_hash_from_merkle_roots(A_root, B_root, key_tensor, ch_A, ch_B,
@@ -186,7 +242,7 @@ def pearl_gemm_noisy(a, b, scale_a, scale_b, out_dtype, job: MiningJob,
                  EAR_R_major=EAR_R, EBL_R_major=EBL_R, EAR_K_major=EAR_K, EBL_K_major=EBL_K,
                  AxEBL_fp16=A_E_BL, EARxBpEB_fp16=EARxBpEB, ApEA=ApEA, BpEB=BpEB, A_scales=scale_a,
                  B_scales=scale_b, C=C, host_signal_header_pinned=header, host_signal_sync=sync,
-                 pow_target=P.make_pow_target_tensor(job.pow_target, device),
+                 pow_target=target_tensor,
                  pow_key=ch_A.view(torch.uint32), tile_size_m=config.tile_size_m,
                  tile_size_n=config.tile_size_n, tile_size_k=config.tile_size_k, run_noising_A=True,
                  run_noising_B=True, skip_reduction=False, skip_denoising=False, hits=hits)
@@ -211,11 +267,16 @@ class PearlLinear:
         smooth = getattr(layer, "smooth_quant_scale", None)
         block = int(getattr(layer, "hadamard_block_size", NO_HADAMARD_BLOCK_SIZE))
         if self.mining_enabled:
+            k, n = x.shape[-1], w_q.shape[0]
+            m = x.numel() // k
+            noisy = self.config.should_use_noisy_gemm(m, n, k) and self.job is not None
+            # the weight's commitment root does not depend on x: hash it beside the quantization
+            b_root = (_tensor_root_async(w_q.contiguous().view(torch.uint8), _job_tensors(self.job, x.device)[0])
+                      if noisy else None)
             x_q, x_s, _ = quant_7bit(x, smooth_scale=smooth, block_size=block)
-            m, k, n = x_q.shape[0], x_q.shape[1], w_q.shape[0]
-            if self.config.should_use_noisy_gemm(m, n, k) and self.job is not None:
+            if noisy:
                 C, mined = pearl_gemm_noisy(x_q.contiguous(), w_q.contiguous(), x_s.squeeze(-1),
-                                            w_s.reshape(-1), x.dtype, self.job, self.config)
+                                            w_s.reshape(-1), x.dtype, self.job, self.config, b_root=b_root)
                 self.mined.append(mined)
                 return C
             return pearl_gemm_vanilla(x_q.contiguous(), w_q.contiguous(), x_s.squeeze(-1),
@@ -276,9 +337,9 @@ def prepare_moe_noising(A_q, A_scales, topk_ids, B_stacked, num_experts: int, jo
     rows_b = B_stacked.shape[0]
     r = config.noise_rank
     top_k = topk_ids.shape[1]
-    key = _u8(job.hash_key, device)
+    key, target_tensor = _job_tensors(job, device)
+    B_hash, b_ready = _tensor_root_async(B_stacked.contiguous().view(torch.uint8), key)
     A_hash = _tensor_root(A_q.contiguous().view(torch.uint8), key)
-    B_hash = _tensor_root(B_stacked.contiguous().view(torch.uint8), key)
     salted = (num_tokens, rows_b // num_experts) if job.salted_seeds else None
     slots = num_tokens * top_k
     routing_data = torch.empty(slots, dtype=torch.int32, device=device)
@@ -294,13 +355,14 @@ def prepare_moe_noising(A_q, A_scales, topk_ids, B_stacked, num_experts: int, jo
     offsets_hash = _tensor_root(routing_offsets.view(torch.uint8).reshape(1, -1), key)
     ch_A = torch.empty(32, device=device, dtype=torch.uint8)
     ch_B = torch.empty(32, device=device, dtype=torch.uint8)
+    torch.cuda.current_stream(device).wait_event(b_ready)
     P.commitment_hash_from_merkle_roots(A_hash, B_hash, key, ch_A, ch_B, routing_root=routing_hash,
                                         offsets_hash=offsets_hash, salted_dims=salted)
     EAL, EAR_R, EBL_R, EAR_K, EBL_K, EBR, EAL_fp16, EBR_fp16 = generate_noise_factors(
         num_tokens, rows_b, hidden, r, ch_A, ch_B, device)
     return MoENoiseContext(ch_A, ch_B, EAL, EAL_fp16, EAR_R, EBL_R, EAR_K, EBL_K, EBR, EBR_fp16,
                            routing_data, routing_hash, offsets_hash, layout,
-                           P.make_pow_target_tensor(job.pow_target, device), ch_A.view(torch.uint32), r)
+                           target_tensor, ch_A.view(torch.uint32), r)
 
 
 def permute_a_side_to_expert_order(layout: MoERoutingLayout, A_q, A_scales, EAL, EAL_fp16):
