@@ -44,20 +44,22 @@ __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return
 template <>
 __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
 
-// Loads vector `vec` (8 elements) of `row`, applies the Hadamard transform of
-// width a.block and the smooth scale.  Every lane of the warp must call it
-// with the same `iter` (the butterflies shuffle across lanes).
+// The raw 16 bytes of vector `vec` (8 elements) of `row` (zero when invalid).
 template <typename T>
-__device__ __forceinline__ void load_vec(const QuantArgs& a, int row, int vec, bool valid, float* v) {
-  if (valid) {
-    const uint4 raw = *reinterpret_cast<const uint4*>(static_cast<const T*>(a.x) + int64_t(row) * a.n + 8 * vec);
-    const T* e = reinterpret_cast<const T*>(&raw);
+__device__ __forceinline__ uint4 load_raw(const QuantArgs& a, int row, int vec, bool valid) {
+  if (!valid) return make_uint4(0u, 0u, 0u, 0u);
+  return *reinterpret_cast<const uint4*>(static_cast<const T*>(a.x) + int64_t(row) * a.n + 8 * vec);
+}
+
+// Vector `vec` of `row` from its raw bytes: the Hadamard transform of width
+// a.block and the smooth scale.  Every lane of the warp must call it with the
+// same `iter` (the butterflies shuffle across lanes).
+template <typename T>
+__device__ __forceinline__ void vec_from_raw(const QuantArgs& a, int row, int vec, bool valid, uint4 raw,
+                                             float* v) {
+  const T* e = reinterpret_cast<const T*>(&raw);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = to_f32<T>(e[i]);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = 0.f;
-  }
+  for (int i = 0; i < 8; ++i) v[i] = valid ? to_f32<T>(e[i]) : 0.f;
   if (a.block > 0) {
 #pragma unroll
     for (int s = 1; s < 8; s <<= 1) {  // butterflies inside the 8-element vector
@@ -87,6 +89,11 @@ __device__ __forceinline__ void load_vec(const QuantArgs& a, int row, int vec, b
     v[0] *= s0.x; v[1] *= s0.y; v[2] *= s0.z; v[3] *= s0.w;
     v[4] *= s1.x; v[5] *= s1.y; v[6] *= s1.z; v[7] *= s1.w;
   }
+}
+
+template <typename T>
+__device__ __forceinline__ void load_vec(const QuantArgs& a, int row, int vec, bool valid, float* v) {
+  vec_from_raw<T>(a, row, vec, valid, load_raw<T>(a, row, vec, valid), v);
 }
 
 template <typename T>
@@ -128,6 +135,73 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const QuantAr
   }
 }
 
+// Rows of at most kIters * kThreads * 8 elements: the row's raw bytes stay in
+// registers between the max pass and the rounding pass, so it is read from
+// memory once, with all of a thread's loads in flight together; the transform
+// is recomputed for the rounding pass (the same operations in the same order
+// as quant_rows_kernel, so the same bytes come out).
+template <typename T, int kIters, int kThreads>
+__global__ void __launch_bounds__(kThreads, 1024 / kThreads) quant_rows_reg_kernel(const QuantArgs a) {
+  __shared__ float warp_max[kThreads / 32];
+  const int row = blockIdx.x;
+  const int nvec = a.n / 8;
+  uint4 raw[kIters];
+#pragma unroll
+  for (int it = 0; it < kIters; ++it) {  // every load of the row in flight at once
+    const int vec = it * kThreads + threadIdx.x;
+    raw[it] = load_raw<T>(a, row, vec, vec < nvec);
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int it = 0; it < kIters; ++it) {
+    const int vec = it * kThreads + threadIdx.x;
+    float v[8];
+    vec_from_raw<T>(a, row, vec, vec < nvec, raw[it], v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x / 32] = amax;
+  __syncthreads();
+  amax = 0.f;
+#pragma unroll
+  for (int w = 0; w < kThreads / 32; ++w) amax = fmaxf(amax, warp_max[w]);
+  const float inv = a.max_val / (amax + 1e-30f);
+  if (threadIdx.x == 0) a.scales[row] = amax * (1.0f / a.max_val);
+#pragma unroll
+  for (int it = 0; it < kIters; ++it) {
+    const int vec = it * kThreads + threadIdx.x;
+    float v[8];
+    vec_from_raw<T>(a, row, vec, vec < nvec, raw[it], v);  // the same values again: no second read
+    if (vec < nvec) {
+      uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float q = fminf(fmaxf(rintf(v[i] * inv), -a.max_val), a.max_val);
+        packed[i / 4] |= (uint32_t(int32_t(q)) & 0xFFu) << (8 * (i % 4));
+      }
+      *reinterpret_cast<uint2*>(a.xq + int64_t(row) * a.n + 8 * vec) = make_uint2(packed[0], packed[1]);
+    }
+  }
+}
+
+template <typename T>
+void launch_quant(const QuantArgs& a, cudaStream_t s) {
+  // 1024 resident threads per SM, each holding at most four 16-byte vectors
+  const int nvec = a.n / 8;
+  if (nvec <= 256)
+    quant_rows_reg_kernel<T, 1, 256><<<a.m, 256, 0, s>>>(a);
+  else if (nvec <= 512)
+    quant_rows_reg_kernel<T, 2, 256><<<a.m, 256, 0, s>>>(a);
+  else if (nvec <= 1024)
+    quant_rows_reg_kernel<T, 4, 256><<<a.m, 256, 0, s>>>(a);
+  else if (nvec <= 2048)
+    quant_rows_reg_kernel<T, 4, 512><<<a.m, 512, 0, s>>>(a);
+  else
+    quant_rows_kernel<T><<<a.m, kQuantThreads, 0, s>>>(a);
+}
+
 }  // namespace
 }  // namespace pb2
 
@@ -163,8 +237,8 @@ extern "C" int pb2_quantize(const pb2_quant_params* pp, void* stream) {
   a.max_val = float(p.max_val);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (p.x_is_fp16)
-    quant_rows_kernel<__half><<<a.m, kQuantThreads, 0, s>>>(a);
+    launch_quant<__half>(a, s);
   else
-    quant_rows_kernel<__nv_bfloat16><<<a.m, kQuantThreads, 0, s>>>(a);
+    launch_quant<__nv_bfloat16>(a, s);
   return launch_status();
 }

@@ -103,6 +103,25 @@ def test_quantize_matches_reference_math(dtype, block, smooth):
     torch.testing.assert_close(xs.cpu(), s_ref, rtol=1e-5, atol=0)
 
 
+@pytest.mark.parametrize("n", [8, 1024, 2056, 4096, 8192, 14336, 16384, 20480])
+@pytest.mark.parametrize("block", [0, 128])
+def test_quantize_row_lengths(n, block):
+    """Every row-length class of the kernel (the row kept in registers for up
+    to 1, 2, 4 or 8 vectors per thread, two passes over memory beyond)."""
+    if block and n % block:
+        pytest.skip("block must divide the row")
+    g = torch.Generator().manual_seed(n + block)
+    m = 64
+    x = (torch.randn(m, n, generator=g) * 3).to(torch.bfloat16)
+    xq = torch.empty(m, n, dtype=torch.int8, device="cuda")
+    xs = torch.empty(m, 1, dtype=torch.float32, device="cuda")
+    pg.quantization.quantize(x.cuda(), xq, xs, smooth_scale=None, max_val=63, block_size=block)
+    q_ref, s_ref = _ref_quant(x, None, 63, block)
+    diff = (xq.cpu().int() - q_ref.int()).abs()
+    assert int(diff.max()) <= 1 and float((diff > 0).float().mean()) < 1e-5
+    torch.testing.assert_close(xs.cpu(), s_ref, rtol=1e-5, atol=0)
+
+
 # ------------------------------------------------------------ dense layer ---
 def _job(seed, frac=0.02, salted=True):
     key = bytes(np.random.default_rng(seed).integers(0, 256, 32, dtype=np.uint8))
