@@ -188,12 +188,13 @@ __global__ void __launch_bounds__(kThreads, 1024 / kThreads) quant_rows_reg_kern
 
 template <typename T>
 void launch_quant(const QuantArgs& a, cudaStream_t s) {
-  // 1024 resident threads per SM, each holding at most four 16-byte vectors
+  // Four 16-byte vectors per thread and 1024 resident threads per SM: 64 KB
+  // of each SM's loads in flight whatever the row length.
   const int nvec = a.n / 8;
   if (nvec <= 256)
-    quant_rows_reg_kernel<T, 1, 256><<<a.m, 256, 0, s>>>(a);
+    quant_rows_reg_kernel<T, 4, 64><<<a.m, 64, 0, s>>>(a);
   else if (nvec <= 512)
-    quant_rows_reg_kernel<T, 2, 256><<<a.m, 256, 0, s>>>(a);
+    quant_rows_reg_kernel<T, 4, 128><<<a.m, 128, 0, s>>>(a);
   else if (nvec <= 1024)
     quant_rows_reg_kernel<T, 4, 256><<<a.m, 256, 0, s>>>(a);
   else if (nvec <= 2048)
