@@ -63,6 +63,28 @@ PB2_API const char* pb2_last_cuda_error(void);
 /* ABI version of the loaded library (PB2_ABI_VERSION). */
 PB2_API int pb2_abi_version(void);
 
+/* ------------------------------------------------------ bounded waits -----
+ * No reference counterpart: the reference's kernels wait without limit (its
+ * first-hit lock spins, pow_utils.hpp:267-269).  Every device-side wait of
+ * these kernels (mbarrier phases, drains, cluster handshakes) gives up after
+ * a budget of SM clock cycles, records PB2_ERR_DEVICE_TIMEOUT in the error
+ * word of host_signal_sync and unwinds, so a stalled pipeline ends the
+ * kernel with a status instead of holding the GPU.
+ * pb2_set_wait_budget_cycles sets the budget that later launches of the
+ * mined GEMM's main kernel (pb2_noisy_gemm, pb2_gemm) take, for the whole
+ * process; cycles <= 0 restores the default (about one second).  Returns the
+ * previous budget.  Launches already queued keep the budget they were
+ * given.  The noising kernels always keep the default: their K-split
+ * clusters read one another's shared memory until an exit handshake, which a
+ * short budget must not cut.
+ * pb2_wait_selftest launches one small kernel whose two warps wait on
+ * mbarriers that nothing completes, with `budget_cycles`
+ * (0 < budget_cycles <= the default): both waits run out, the error word
+ * becomes PB2_ERR_DEVICE_TIMEOUT and the kernel returns. */
+#define PB2_DEFAULT_WAIT_BUDGET_CYCLES 2000000000LL
+PB2_API int64_t pb2_set_wait_budget_cycles(int64_t cycles);
+PB2_API int pb2_wait_selftest(int device, int64_t budget_cycles, void* host_signal_sync, void* stream);
+
 /* ----------------------------------------------------------- tensor_hash ---
  * Replaces tensor_hash (tensor_hash_api.hpp:45-120; kernels
  * merkle_tree_roots_kernel.hpp, compute_blake_mt_kernel.hpp,
@@ -163,9 +185,16 @@ PB2_API int64_t pb2_build_routing_data_scratchpad_bytes(int64_t numel);
  * (quantization_operators.py:72-100): per row of x (m, n) bf16 or fp16,
  * optional block Walsh-Hadamard transform of width block_size (0 = none; else
  * a power of two in [8, 256] dividing n), times smooth (1 x n, or m x n when
- * smooth_per_row; may be NULL), then xq = rint(v * max_val / amax) clamped to
- * +-max_val and scales[row] = amax / max_val.  n % 8 == 0; x and smooth
- * 16-byte aligned, xq 8-byte aligned. */
+ * smooth_per_row; may be NULL), then xq = rint(v * inv) clamped to +-max_val
+ * with inv = max_val * rcp.approx.ftz(amax + 1e-30), and scales[row] =
+ * amax * fl(1 / max_val) (hadamard.py:443-466, the same float32 steps).
+ * x and smooth 16-byte aligned, xq 8-byte aligned.
+ * Narrower than the reference: n % 8 == 0 (16-byte row vectors; model
+ * widths always are) and block_size >= 8.  The reference's layout puts
+ * gcd(n, 8) elements in a thread, and for a block narrower than that its
+ * per-block negation index k / vecsize is zero (hadamard.py:505-511), so
+ * widths 2 and 4 have no well-defined reference result to match; both
+ * cases return PB2_ERR_UNSUPPORTED_CONFIG. */
 typedef struct pb2_quant_params {
   int device;
   const void* x;
@@ -179,6 +208,12 @@ typedef struct pb2_quant_params {
   int block_size;
 } pb2_quant_params;
 PB2_API int pb2_quantize(const pb2_quant_params* p, void* stream);
+/* Test aid, no reference counterpart: out[i] = rcp.approx.ftz.f32(in[i]) on
+ * `device`, the approximate reciprocal pb2_quantize takes as the reference's
+ * kernel does (cute.arch.rcp_approx).  PTX bounds its error (1 ulp) but does
+ * not fix its last bit, so a CPU restatement of the quantizer reads it from
+ * the device.  in and out hold n floats on `device`. */
+PB2_API int pb2_rcp_approx_f32(int device, const float* in, float* out, int64_t n, void* stream);
 
 /* ---------------------------------------------------------- scatter_rows ---
  * dst[indices[i]] = src[i] for i < rows, rows of row_bytes bytes (a multiple

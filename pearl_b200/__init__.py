@@ -39,6 +39,8 @@ from .pearl_gemm_interface import (
     tensor_hash,
 )
 from . import moe
+from . import quantization
+from . import device_waits
 from . import ops  # noqa: F401  (registers torch.ops.pearl_gemm.*)
 
 __all__ = [
@@ -58,6 +60,8 @@ __all__ = [
     "get_host_signal_sync_size",
     "inner_hash",
     "moe",
+    "quantization",
+    "device_waits",
     "kEALScaleFactorDenoise",
     "kEBRScaleFactorDenoise",
     "make_pow_target_tensor",

@@ -34,8 +34,10 @@ EXPORTED = [
     "pb2_noisy_gemm_static_scratch", "pb2_tensor_hash", "pb2_required_scratchpad_bytes",
     "pb2_commitment_hash_from_merkle_roots", "pb2_build_routing_data",
     "pb2_build_routing_data_scratchpad_bytes", "pb2_quantize", "pb2_scatter_rows",
-    "pb2_merkle_layers", "pb2_merkle_nodes",
+    "pb2_merkle_layers", "pb2_merkle_nodes", "pb2_set_wait_budget_cycles", "pb2_wait_selftest",
+    "pb2_rcp_approx_f32",
 ]
+DEFAULT_WAIT_BUDGET_CYCLES = 2000000000
 
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -154,6 +156,12 @@ def load() -> ctypes.CDLL:
         L.pb2_status_string.argtypes = [ctypes.c_int]
         L.pb2_last_cuda_error.restype = ctypes.c_char_p
         L.pb2_abi_version.restype = ctypes.c_int
+        L.pb2_set_wait_budget_cycles.restype = _i64
+        L.pb2_set_wait_budget_cycles.argtypes = [_i64]
+        L.pb2_wait_selftest.restype = ctypes.c_int
+        L.pb2_wait_selftest.argtypes = [ctypes.c_int, _i64, _vp, _vp]
+        L.pb2_rcp_approx_f32.restype = ctypes.c_int
+        L.pb2_rcp_approx_f32.argtypes = [ctypes.c_int, _vp, _vp, _i64, _vp]
         _lib = L
     return _lib
 

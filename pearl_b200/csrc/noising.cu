@@ -48,6 +48,7 @@ struct NoisingArgs {
   int8_t* XpE;
   void* proj;
   SignalSync* sync;
+  long long wait_budget;  // SM cycles a device-side wait may spin (pb2_set_wait_budget_cycles)
 };
 
 struct NSmem {
@@ -67,12 +68,18 @@ struct NSmem {
   int abort_flag;
 };
 
-__device__ __forceinline__ bool wait_cluster_bounded(uint64_t* bar, uint32_t parity) {
+// Cluster-scope wait with one verdict for the whole warp (the callers go on
+// to warp-wide code).
+__device__ __forceinline__ bool wait_cluster_bounded(uint64_t* bar, uint32_t parity, long long budget) {
   long long t0 = clock64();
+  bool ok = true;
   while (!mbar_test_cluster(bar, parity)) {
-    if (clock64() - t0 > kWaitBudgetCycles) return false;
+    if (clock64() - t0 > budget) {
+      ok = false;
+      break;
+    }
   }
-  return true;
+  return __all_sync(0xffffffffu, ok);
 }
 
 // Byte offset of 16-byte chunk `ch` of row `row` in a 128-byte-row tile with
@@ -180,7 +187,7 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
       int i = 0;
       for (; i < nkb; ++i) {
         const int s = i % kStages;
-        if (!mbar_wait_warp(&S.empty[s], ((i / kStages) & 1) ^ 1, abort_flag, a.sync)) break;
+        if (!mbar_wait_warp(&S.empty[s], ((i / kStages) & 1) ^ 1, abort_flag, a.sync, a.wait_budget)) break;
         uint8_t* st = stages + s * kStageSlot;
         const int k = (kb0 + i) * NKB;
         if (leader) {
@@ -205,7 +212,7 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
     // The whole warp runs the issue loop; one elected lane issues each MMA
     // and commit (the *_warp forms).
     {
-      bool ok = mbar_wait_warp(&S.el_full, 0, abort_flag, a.sync);
+      bool ok = mbar_wait_warp(&S.el_full, 0, abort_flag, a.sync, a.wait_budget);
       const uint32_t el = smem_u32(el_buf);
       // projection of k-block j: D2_h += Xs_h[j] . E_kmajor[j]^T
       auto mma2 = [&](int j) {
@@ -225,7 +232,7 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
       auto proj = [&](int j) -> bool {
         const int s = j % kStages;
         uint64_t* ready = kB ? &S.xp_ready[s] : &S.full_x[s];
-        if (!mbar_wait_warp(ready, (j / kStages) & 1, abort_flag, a.sync)) return false;
+        if (!mbar_wait_warp(ready, (j / kStages) & 1, abort_flag, a.sync, a.wait_budget)) return false;
         tc_fence_after();
         mma2(j);
         if (!kB) umma_commit_warp(&S.x_free[s]);
@@ -238,8 +245,8 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
       // waits for it).
       for (int i = 0; i < nkb && ok; ++i) {
         const int s = i % kStages;
-        if (!(ok = mbar_wait_warp(&S.full_e[s], (i / kStages) & 1, abort_flag, a.sync))) break;
-        if (i >= 1 && !(ok = mbar_wait_warp(&S.d1_empty, (i - 1) & 1, abort_flag, a.sync))) break;
+        if (!(ok = mbar_wait_warp(&S.full_e[s], (i / kStages) & 1, abort_flag, a.sync, a.wait_budget))) break;
+        if (i >= 1 && !(ok = mbar_wait_warp(&S.d1_empty, (i - 1) & 1, abort_flag, a.sync, a.wait_budget))) break;
         tc_fence_after();
         {
           const uint64_t bd = sdesc_kmajor<R>(smem_u32(stages + s * kStageSlot + kXBytes));
@@ -273,7 +280,7 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
     bool ok = true;
     for (int i = 0; i < nkb && ok; ++i) {
       const int s = i % kStages;
-      if (!(ok = mbar_wait(&S.d1_full, i & 1, abort_flag, a.sync))) break;
+      if (!(ok = mbar_wait_warp(&S.d1_full, i & 1, abort_flag, a.sync, a.wait_budget))) break;
       tc_fence_after();
       // The noise bytes of this thread's row, packed while X is in flight.
       uint32_t nz[16];
@@ -290,8 +297,8 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
         for (int w = 0; w < 16; ++w) nz[w] = low_bytes4(v[w >> 3] + 4 * (w & 7));
       }
       // X landed (and, for noise_A, the projection has read it).
-      if (!(ok = mbar_wait(&S.full_x[s], (i / kStages) & 1, abort_flag, a.sync))) break;
-      if (!kB && !(ok = mbar_wait(&S.x_free[s], (i / kStages) & 1, abort_flag, a.sync))) break;
+      if (!(ok = mbar_wait_warp(&S.full_x[s], (i / kStages) & 1, abort_flag, a.sync, a.wait_budget))) break;
+      if (!kB && !(ok = mbar_wait_warp(&S.x_free[s], (i / kStages) & 1, abort_flag, a.sync, a.wait_budget))) break;
       uint8_t* xt = stages + s * kStageSlot;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -333,7 +340,7 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
     constexpr int kRowsPerIter = 32 / kChunks;  // rows a warp covers per pass
     int32_t* red = reinterpret_cast<int32_t*>(stages);
     const int nr = a.use_cluster ? a.ks : 1;
-    ok = ok && mbar_wait(&S.d2_full, 0, abort_flag, a.sync);
+    ok = ok && mbar_wait_warp(&S.d2_full, 0, abort_flag, a.sync, a.wait_budget);
     // The partial overwrites the ring: every epilogue warp is done with it.
     ok = named_barrier_and(1, 32 * kEpiWarps, ok);
     if (a.use_cluster) {
@@ -363,8 +370,8 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
           mbar_arrive(&S.red_ready);
         }
       }
-      ok = a.use_cluster ? wait_cluster_bounded(&S.red_ready, 0)
-                         : mbar_wait(&S.red_ready, 0, abort_flag, a.sync);
+      ok = a.use_cluster ? wait_cluster_bounded(&S.red_ready, 0, a.wait_budget)
+                         : mbar_wait_warp(&S.red_ready, 0, abort_flag, a.sync, a.wait_budget);
     }
     if (ok) {
       const int per = (NM + nr - 1) / nr;
@@ -417,7 +424,7 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
         __syncwarp();
         if (lane == 0)
           for (int r = 0; r < nr; ++r) mbar_arrive_remote(mapa(&S.red_done, uint32_t(r)));
-        if (!wait_cluster_bounded(&S.red_done, 0)) ok = false;
+        if (!wait_cluster_bounded(&S.red_done, 0, a.wait_budget)) ok = false;
       }
     }
   }
@@ -541,6 +548,11 @@ int prepare_noising(const pb2_noising_params& p, bool b_side, NoisingArgs* out) 
   a.XpE = static_cast<int8_t*>(p.XpE);
   a.proj = p.proj;
   a.sync = static_cast<SignalSync*>(p.host_signal_sync);
+  // Always the default budget, never the process-wide one: a CTA of a
+  // K-split cluster leaves only after its peers have read its partial (the
+  // red_done handshake), and a budget short enough to cut that wait would
+  // let peers read the shared memory of a CTA that has left.
+  a.wait_budget = kWaitBudgetCycles;
   return PB2_OK;
 }
 

@@ -76,6 +76,7 @@ struct MainArgs {
   long long hit_cap;
   uint32_t* transcripts;
   uint32_t* digests;
+  long long wait_budget;  // SM cycles a device-side wait may spin (pb2_set_wait_budget_cycles)
 };
 
 struct Smem {
@@ -287,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
             const int m0 = s ? mb : ma, n0 = s ? nb : na;
             for (int st = 0; st < stages_per_unit; ++st, ++it) {
               const int j = it % kStages;
-              if (!(ok = mbar_wait_warp(&S.empty[j], ((it / kStages) & 1) ^ 1, abort_flag, a.sync))) break;
+              if (!(ok = mbar_wait_warp(&S.empty[j], ((it / kStages) & 1) ^ 1, abort_flag, a.sync, a.wait_budget))) break;
               uint8_t* sa = stage_mem + j * kStageBytes;
               const int kbyte = u * unit_k + st * BK;
               if (leader) {
@@ -305,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
               const int m0 = s ? mb : ma, n0 = s ? nb : na;
               for (int st = 0; st < stages_per_unit; ++st, ++it) {
                 const int j = it % kStages;
-                if (!(ok = mbar_wait_warp(&S.empty[j], ((it / kStages) & 1) ^ 1, abort_flag, a.sync))) break;
+                if (!(ok = mbar_wait_warp(&S.empty[j], ((it / kStages) & 1) ^ 1, abort_flag, a.sync, a.wait_budget))) break;
                 uint8_t* sa = stage_mem + j * kStageBytes;
                 const int ds = d * stages_per_unit + st;
                 const int col = (ds % den_stages_per_product) * (BK / 2);
@@ -348,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
       const uint32_t sbase = smem_u32(stage_mem);
       auto acquire = [&](int s) -> bool {
         if (!bit(pend, s)) return true;
-        if (!mbar_wait_warp(&S.acc_empty[s], bit(empar, s), abort_flag, a.sync)) return false;
+        if (!mbar_wait_warp(&S.acc_empty[s], bit(empar, s), abort_flag, a.sync, a.wait_budget)) return false;
         empar ^= 1u << s;
         pend &= ~(1u << s);
         tc_fence_after();
@@ -356,12 +357,12 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
       };
       auto main_unit = [&](int s, int u) {
         // Operands first (usually resident already), then the slot.
-        if (!(ok = mbar_wait_warp(&S.full[it % kStages], (it / kStages) & 1, abort_flag, a.sync))) return;
+        if (!(ok = mbar_wait_warp(&S.full[it % kStages], (it / kStages) & 1, abort_flag, a.sync, a.wait_budget))) return;
         if ((kReduce || u == 0) && !(ok = acquire(s))) return;
         const uint32_t dt = tmem + 256 * s;
         for (int st = 0; st < stages_per_unit; ++st, ++it) {
           const int j = it % kStages;
-          if (st > 0 && !(ok = mbar_wait_warp(&S.full[j], (it / kStages) & 1, abort_flag, a.sync))) return;
+          if (st > 0 && !(ok = mbar_wait_warp(&S.full[j], (it / kStages) & 1, abort_flag, a.sync, a.wait_budget))) return;
           tc_fence_after();
           const uint64_t ad = sdesc_kmajor<BK>(sbase + j * kStageBytes);
           const uint64_t bd = sdesc_kmajor<BK>(sbase + j * kStageBytes + kAStage);
@@ -381,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
         const uint32_t dt = tmem + 256 * s;
         for (int st = 0; st < stages_per_unit; ++st, ++it) {
           const int j = it % kStages;
-          if (!(ok = mbar_wait_warp(&S.full[j], (it / kStages) & 1, abort_flag, a.sync))) return;
+          if (!(ok = mbar_wait_warp(&S.full[j], (it / kStages) & 1, abort_flag, a.sync, a.wait_budget))) return;
           tc_fence_after();
           const uint64_t ad = sdesc_kmajor<BK>(sbase + j * kStageBytes);
           const uint64_t bd = sdesc_kmajor<BK>(sbase + j * kStageBytes + kAStage);
@@ -462,10 +463,11 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
       const bool is_main = u < nmain;
       const bool last_main = u == nmain - 1;
       if (kReduce && is_main) {
-        if (!(ok = mbar_wait(&S.empty[last_stage % kStages], (last_stage / kStages) & 1, abort_flag, a.sync)))
+        if (!(ok = mbar_wait_warp(&S.empty[last_stage % kStages], (last_stage / kStages) & 1, abort_flag, a.sync,
+                                  a.wait_budget)))
           return;
       } else {
-        if (!(ok = mbar_wait(&S.acc_full[s], bit(fpar, s), abort_flag, a.sync))) return;
+        if (!(ok = mbar_wait_warp(&S.acc_full[s], bit(fpar, s), abort_flag, a.sync, a.wait_budget))) return;
         fpar ^= 1u << s;
       }
       tc_fence_after();
@@ -507,7 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
         // A tile's first chunk reuses the buffer of two rounds ago: the hash
         // warps must have cleared it.
         if (u == 0 && round >= 2 &&
-            !(ok = mbar_wait_idle(&S.xfree[b], ((round >> 1) - 1) & 1, abort_flag, a.sync)))
+            !(ok = mbar_wait_idle_warp(&S.xfree[b], ((round >> 1) - 1) & 1, abort_flag, a.sync, a.wait_budget)))
           return false;
         uint32_t* tw = xbuf + b * (16 * 256) + w * 256 + lane_tile;
         atomicXor(tw, __funnelshift_l(f0, f0, rot));
@@ -622,7 +624,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
     bool ok = true;
     auto hash_buffer = [&](auto slot, int round, int tm, int tn) {
       const int b = 2 * decltype(slot)::value + (round & 1);
-      if (!(ok = mbar_wait_idle(&S.xready[b], (round >> 1) & 1, abort_flag, a.sync))) return;
+      if (!(ok = mbar_wait_idle_warp(&S.xready[b], (round >> 1) & 1, abort_flag, a.sync, a.wait_budget))) return;
       const int tm128 = 2 * tm + int(rank);
 #pragma unroll 1
       for (int i = 0; i < 4; ++i) {
@@ -733,7 +735,8 @@ bool al16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
 
 }  // namespace
 
-int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStream_t s) {
+// Every check of the main kernel's arguments that needs no CUDA call.
+int check_main_args(const pb2_gemm_params& p, bool reduce, bool denoise) {
   if (p.m <= 0 || p.n <= 0 || p.k <= 0) return PB2_ERR_INVALID_ARGUMENT;
   if (p.tile_size_m != BMC || p.tile_size_n != BN || p.tile_size_k != kTileK) return PB2_ERR_UNSUPPORTED_CONFIG;
   if (p.cluster_size_m != 1 || p.cluster_size_n != 1) return PB2_ERR_UNSUPPORTED_CONFIG;
@@ -747,9 +750,23 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
   if (reduce && (!p.host_signal_sync || !p.pow_target || !p.pow_key)) return PB2_ERR_INVALID_ARGUMENT;
   if (denoise && (!p.EAL_fp16 || !p.EBR_fp16 || !p.AxEBL_fp16 || !p.EARxBpEB_fp16))
     return PB2_ERR_INVALID_ARGUMENT;
-  const bool debug = reduce && p.enable_debug;
-  if (debug && !p.inner_hash_counter) return PB2_ERR_INVALID_ARGUMENT;
+  if (reduce && p.enable_debug && !p.inner_hash_counter) return PB2_ERR_INVALID_ARGUMENT;
   if ((p.transcripts || p.digests) && (p.m % 16 != 0 || p.n % 256 != 0)) return PB2_ERR_INVALID_ARGUMENT;
+  return PB2_OK;
+}
+
+// Every argument check of pb2_noisy_gemm that needs no CUDA call: a call
+// these reject has queued no work.
+int check_noisy_gemm_args(const pb2_gemm_params& p) {
+  if (p.run_noising_a && (!p.A || !p.EAL || !p.EAR_R_major || !p.EBL_K_major)) return PB2_ERR_INVALID_ARGUMENT;
+  if (p.run_noising_b && (!p.B || !p.EBR || !p.EAR_K_major || !p.EBL_R_major)) return PB2_ERR_INVALID_ARGUMENT;
+  return check_main_args(p, !p.skip_reduction, !p.skip_denoising);
+}
+
+int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStream_t s) {
+  int cst = check_main_args(p, reduce, denoise);
+  if (cst) return cst;
+  const bool debug = reduce && p.enable_debug;
 
   // 128-byte stages (128-byte swizzle) unless R = 64, where 64-byte stages
   // (64-byte swizzle) keep a transcript chunk a whole number of stages.
@@ -795,6 +812,7 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
   a.hit_cap = p.hits ? p.hit_capacity : 0;
   a.transcripts = p.transcripts;
   a.digests = p.digests;
+  a.wait_budget = wait_budget_cycles();
 
   // Operand stages per unit: a unit is R bytes of K with transcript or
   // denoise (R = 64: one 64-byte stage; R = 128: one; R = 256: two), else
@@ -815,8 +833,9 @@ extern "C" int pb2_noisy_gemm(const pb2_gemm_params* pp, void* stream) {
   if (!pp) return PB2_ERR_INVALID_ARGUMENT;
   const pb2_gemm_params& p = *pp;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int st = set_device(p.device);
+  int st = check_noisy_gemm_args(p);
   if (st) return st;
+  if ((st = set_device(p.device))) return st;
   pb2_noising_params qa{}, qb{};
   if (p.run_noising_a) {
     if (!p.A || !p.EAL || !p.EAR_R_major || !p.EBL_K_major) return PB2_ERR_INVALID_ARGUMENT;

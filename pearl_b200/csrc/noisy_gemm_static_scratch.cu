@@ -63,17 +63,20 @@ extern "C" int pb2_noisy_gemm_static_scratch(const pb2_gemm_params* pp, void* st
   const int64_t b_words = p.run_noising_b ? p.n * p.r : 0;
   if (a_words + b_words > kScratchWords) return PB2_ERR_SCRATCH_LIMIT;
 
-  int st = pb2::set_device(p.device);
+  // Every argument error is returned before the clear below is queued: a
+  // rejected call must not touch the array an earlier call may still use.
+  int st = pb2::check_noisy_gemm_args(p);
   if (st) return st;
+  if ((st = pb2::set_device(p.device))) return st;
   int32_t* scratch = nullptr;
   if ((st = scratch_on(p.device, &scratch))) return st;
+  pb2_gemm_params q = p;
+  q.AxEBL_int32 = a_words ? scratch : nullptr;
+  q.EARxBpEB_int32 = b_words ? scratch + a_words : nullptr;
   if (a_words + b_words > 0) {
     const cudaError_t e = cudaMemsetAsync(scratch, 0, size_t(a_words + b_words) * sizeof(int32_t),
                                           static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return pb2::cuda_status(e);
   }
-  pb2_gemm_params q = p;
-  q.AxEBL_int32 = a_words ? scratch : nullptr;
-  q.EARxBpEB_int32 = b_words ? scratch + a_words : nullptr;
   return pb2_noisy_gemm(&q, stream);
 }

@@ -45,10 +45,12 @@ struct __align__(128) SignalHeader {
 };
 static_assert(sizeof(SignalHeader) == PB2_HOST_SIGNAL_HEADER_SIZE, "header size");
 
-// Spin budget of every device-side wait, in SM clock cycles (~1 s at the
+// Default spin budget of a device-side wait, in SM clock cycles (~1 s at the
 // B200's clocks).  Nothing legitimate waits longer than microseconds; a wait
-// that runs out records PB2_ERR_DEVICE_TIMEOUT and the kernel unwinds.
-constexpr long long kWaitBudgetCycles = 2000000000LL;
+// that runs out records PB2_ERR_DEVICE_TIMEOUT and the kernel unwinds.  The
+// kernels with pipelined waits take the budget as a launch argument
+// (pb2_set_wait_budget_cycles sets it for the process).
+constexpr long long kWaitBudgetCycles = PB2_DEFAULT_WAIT_BUDGET_CYCLES;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -89,13 +91,13 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 // records the error / raises the CTA abort flag) if the budget runs out or
 // another warp of the CTA already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          SignalSync* sync) {
+                                          SignalSync* sync, long long budget = kWaitBudgetCycles) {
   if (mbar_test(bar, parity)) return true;
   long long t0 = clock64();
   while (true) {
     if (mbar_test(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitBudgetCycles) {
+    if (clock64() - t0 > budget) {
       *abort_flag = 1;
       record_error(sync, PB2_ERR_DEVICE_TIMEOUT);
       return false;
@@ -106,8 +108,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // mbar_wait by every lane of a converged warp, with one verdict for all of
 // them (a lane that ran out of budget makes the whole warp give up).
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                               SignalSync* sync) {
-  const bool ok = mbar_wait(bar, parity, abort_flag, sync);
+                                               SignalSync* sync, long long budget = kWaitBudgetCycles) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, sync, budget);
   return __all_sync(0xffffffffu, ok);
 }
 
@@ -115,19 +117,29 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, v
 // between polls, so the polling does not compete for issue slots and the
 // shared-memory pipe with latency-critical warps).
 __device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                               SignalSync* sync) {
+                                               SignalSync* sync, long long budget = kWaitBudgetCycles) {
   if (mbar_test(bar, parity)) return true;
   long long t0 = clock64();
   while (true) {
     __nanosleep(100);
     if (mbar_test(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitBudgetCycles) {
+    if (clock64() - t0 > budget) {
       *abort_flag = 1;
       record_error(sync, PB2_ERR_DEVICE_TIMEOUT);
       return false;
     }
   }
+}
+
+// mbar_wait_idle with one verdict for the whole (converged) warp.  Warps
+// that go on to warp-collective instructions (tcgen05.ld/st .sync.aligned,
+// __syncwarp, shuffles) wait with a warp-wide verdict, so a lane whose budget
+// ran out a moment before its neighbours' cannot split the warp.
+__device__ __forceinline__ bool mbar_wait_idle_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                    SignalSync* sync, long long budget = kWaitBudgetCycles) {
+  const bool ok = mbar_wait_idle(bar, parity, abort_flag, sync, budget);
+  return __all_sync(0xffffffffu, ok);
 }
 
 // ------------------------------------------------------------------ TMA
@@ -673,6 +685,12 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
 int set_device(int device);
 int sm_count(int device);
 int launch_status();
+// The process-wide wait budget (pb2_set_wait_budget_cycles) for launches.
+long long wait_budget_cycles();
+// Every argument check of pb2_noisy_gemm that needs no CUDA call
+// (noisy_gemm.cu): PB2_OK, or the status pb2_noisy_gemm would return before
+// queueing any work.
+int check_noisy_gemm_args(const pb2_gemm_params& p);
 // PB2_OK for cudaSuccess, else PB2_ERR_CUDA with the error's text recorded
 // for pb2_last_cuda_error.
 int cuda_status(cudaError_t e);

@@ -1,6 +1,7 @@
 // pb2_host.cu -- host-side helpers of the C ABI: tensor-map encoding through
 // the driver entry point (no libcuda link dependency), device selection,
 // status strings and the signalling-buffer sizes.
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -76,6 +77,40 @@ int sm_count(int device) {
 
 int launch_status() { return note_cuda(cudaGetLastError()); }
 
+namespace {
+std::atomic<long long> g_wait_budget{PB2_DEFAULT_WAIT_BUDGET_CYCLES};
+}  // namespace
+
+long long wait_budget_cycles() { return g_wait_budget.load(std::memory_order_relaxed); }
+
+// A minimal kernel that waits on mbarriers nobody arrives at: one warp with
+// the spinning wait, one with the sleeping wait, each with the given budget.
+// Both run out, record PB2_ERR_DEVICE_TIMEOUT in the sync word's error field
+// and return; the kernel ends without any other effect.
+__global__ void wait_selftest_kernel(SignalSync* sync, long long budget) {
+  __shared__ uint64_t never[2];
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&never[0], 1);
+    mbar_init(&never[1], 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int warp = threadIdx.x / 32;
+  // A private abort flag per warp, so each warp's wait runs out on its own
+  // clock rather than seeing the other's abort.
+  volatile int mine = 0;
+  bool ok;
+  if (warp == 0)
+    ok = mbar_wait_warp(&never[0], 0, &mine, sync, budget);
+  else
+    ok = mbar_wait_idle_warp(&never[1], 0, &mine, sync, budget);
+  if (!ok && (threadIdx.x & 31) == 0) atomicAdd(&abort_flag, 1);
+  __syncthreads();
+  if (threadIdx.x == 0 && abort_flag != 2) record_error(sync, PB2_ERR_INVALID_ARGUMENT);
+}
+
 int cuda_status(cudaError_t e) { return note_cuda(e); }
 
 }  // namespace pb2
@@ -108,5 +143,20 @@ const char* pb2_status_string(int status) {
 }
 
 const char* pb2_last_cuda_error(void) { return pb2::g_last_cuda_error; }
+
+int64_t pb2_set_wait_budget_cycles(int64_t cycles) {
+  const long long v = cycles > 0 ? cycles : PB2_DEFAULT_WAIT_BUDGET_CYCLES;
+  return pb2::g_wait_budget.exchange(v);
+}
+
+int pb2_wait_selftest(int device, int64_t budget_cycles, void* host_signal_sync, void* stream) {
+  if (!host_signal_sync || budget_cycles <= 0 || budget_cycles > PB2_DEFAULT_WAIT_BUDGET_CYCLES)
+    return PB2_ERR_INVALID_ARGUMENT;
+  int st = pb2::set_device(device);
+  if (st) return st;
+  pb2::wait_selftest_kernel<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<pb2::SignalSync*>(host_signal_sync), budget_cycles);
+  return pb2::launch_status();
+}
 
 }  // extern "C"

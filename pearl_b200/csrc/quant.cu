@@ -6,8 +6,10 @@
 // Per row: x (bf16 / fp16) -> optional block-diagonal Walsh-Hadamard
 // transform of width k (Sylvester order, scaled by 1/sqrt(k), first element
 // of every block negated: hadamard.py:476-517) -> times the smooth scale ->
-// amax; scale = amax / max_val, q = rint(x * max_val / (amax + 1e-30))
-// clamped to [-max_val, max_val] (hadamard.py:443-466).
+// amax; scale = amax * fl(1 / max_val), q = rint(x * inv) clamped to
+// [-max_val, max_val] with inv = max_val * rcp.approx.ftz(amax + 1e-30)
+// (hadamard.py:443-466): the approximate reciprocal of the reference's
+// kernel, so every rounding step, ties included, lands where it does there.
 //
 // One 256-thread CTA per row, eight elements per thread and 16-byte loads:
 // a k-block is k/8 consecutive threads of one warp, so the cross-element
@@ -16,6 +18,7 @@
 // 2 bytes read and 1 written per element.
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cmath>
 
 #include "pb2_common.cuh"
@@ -35,7 +38,21 @@ struct QuantArgs {
   int block;   // Hadamard width, 0 = none
   float norm;  // 1/sqrt(block), correctly rounded (the reference's constant)
   float max_val;
+  float inv_max_val;  // fl(1 / max_val), the reference's compile-time constant
 };
+
+// rcp.approx.ftz.f32: the reciprocal the reference's quantizer takes
+// (cute.arch.rcp_approx, hadamard.py:446).
+__device__ __forceinline__ float rcp_approx_ftz(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// inv_scale of a row (hadamard.py:443-446).
+__device__ __forceinline__ float inv_scale(const QuantArgs& a, float amax) {
+  return a.max_val * rcp_approx_ftz(amax + 1e-30f);
+}
 
 template <typename T>
 __device__ __forceinline__ float to_f32(T v);
@@ -117,8 +134,8 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const QuantAr
   amax = 0.f;
 #pragma unroll
   for (int w = 0; w < kQuantThreads / 32; ++w) amax = fmaxf(amax, warp_max[w]);
-  const float inv = a.max_val / (amax + 1e-30f);
-  if (threadIdx.x == 0) a.scales[row] = amax * (1.0f / a.max_val);
+  const float inv = inv_scale(a, amax);
+  if (threadIdx.x == 0) a.scales[row] = amax * a.inv_max_val;
   for (int it = 0; it < iters; ++it) {
     const int vec = it * kQuantThreads + threadIdx.x;
     float v[8];
@@ -167,8 +184,8 @@ __global__ void __launch_bounds__(kThreads, 1024 / kThreads) quant_rows_reg_kern
   amax = 0.f;
 #pragma unroll
   for (int w = 0; w < kThreads / 32; ++w) amax = fmaxf(amax, warp_max[w]);
-  const float inv = a.max_val / (amax + 1e-30f);
-  if (threadIdx.x == 0) a.scales[row] = amax * (1.0f / a.max_val);
+  const float inv = inv_scale(a, amax);
+  if (threadIdx.x == 0) a.scales[row] = amax * a.inv_max_val;
 #pragma unroll
   for (int it = 0; it < kIters; ++it) {
     const int vec = it * kThreads + threadIdx.x;
@@ -236,10 +253,31 @@ extern "C" int pb2_quantize(const pb2_quant_params* pp, void* stream) {
   a.block = p.block_size;
   a.norm = p.block_size ? float(1.0 / sqrt(double(p.block_size))) : 1.0f;
   a.max_val = float(p.max_val);
+  a.inv_max_val = float(1.0 / double(p.max_val));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (p.x_is_fp16)
     launch_quant<__half>(a, s);
   else
     launch_quant<__nv_bfloat16>(a, s);
+  return launch_status();
+}
+
+namespace pb2 {
+namespace {
+__global__ void rcp_approx_kernel(const float* in, float* out, int64_t n) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+    out[i] = rcp_approx_ftz(in[i]);
+}
+}  // namespace
+}  // namespace pb2
+
+extern "C" int pb2_rcp_approx_f32(int device, const float* in, float* out, int64_t n, void* stream) {
+  using namespace pb2;
+  if (n < 0 || (n > 0 && (!in || !out))) return PB2_ERR_INVALID_ARGUMENT;
+  int st = set_device(device);
+  if (st) return st;
+  if (n == 0) return PB2_OK;
+  const int blocks = int(std::min<int64_t>((n + 255) / 256, 4096));
+  rcp_approx_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(in, out, n);
   return launch_status();
 }

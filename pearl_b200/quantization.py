@@ -22,8 +22,10 @@ def quantize(
     max_val: int = 63,
     block_size: int = DEFAULT_HADAMARD_BLOCK_SIZE,
 ) -> None:
-    """xq = rint(v * max_val / amax_row(v)) with v = Hadamard_k(x) * smooth
-    (k = block_size, 0 = no transform), xq_scales = amax_row(v) / max_val.
+    """xq = rint(v * inv) with v = Hadamard_k(x) * smooth (k = block_size,
+    0 = no transform), inv = max_val * rcp.approx(amax_row(v) + 1e-30) and
+    xq_scales = amax_row(v) * fl(1 / max_val): the reference's float32 steps
+    (hadamard.py:443-466), so the same bytes come out.
 
     x: (M, N) fp16 / bf16 contiguous; xq: (M, N) int8; xq_scales: (M, 1)
     fp32; smooth_scale: (1, N) broadcast or (M, N) per token, fp32."""
@@ -63,4 +65,20 @@ def quantize(
         _lib.call("pb2_quantize", p, _stream(x.device), "quantize")
 
 
-__all__ = ["quantize", "DEFAULT_HADAMARD_BLOCK_SIZE"]
+def rcp_approx_f32(x: torch.Tensor) -> torch.Tensor:
+    """rcp.approx.ftz.f32 of every element of a float32 CUDA tensor: the
+    approximate reciprocal ``quantize`` takes for its inverse scale, as the
+    reference's kernel does (hadamard.py:446, cute.arch.rcp_approx).  PTX
+    bounds its error to 1 ulp without fixing the last bit, so a CPU
+    restatement of the quantizer reads it from here (a test aid)."""
+    if not x.is_cuda or x.dtype != torch.float32 or not x.is_contiguous():
+        _fail("x must be a contiguous float32 CUDA tensor")
+    out = torch.empty_like(x)
+    with torch.cuda.device(x.device):
+        st = _lib.load().pb2_rcp_approx_f32(_device_index(x), x.data_ptr(), out.data_ptr(), x.numel(),
+                                            _stream(x.device))
+    _lib.check(st, "rcp_approx_f32")
+    return out
+
+
+__all__ = ["quantize", "rcp_approx_f32", "DEFAULT_HADAMARD_BLOCK_SIZE"]

@@ -116,3 +116,35 @@ def test_static_scratch_rejects_oversize_and_caller_buffers():
     assert L.pb2_noisy_gemm_static_scratch(ctypes.byref(q), None) == _lib.PB2_ERR_INVALID_ARGUMENT
     assert L.pb2_noisy_gemm_static_scratch(None, None) == _lib.PB2_ERR_INVALID_ARGUMENT
     assert np.int64(_lib.STATIC_SCRATCH_BYTES) == 8 * 1024 * 1024
+
+
+def _complete_params():
+    """Parameters that pass every argument check (placeholder addresses,
+    16-byte aligned); nothing is launched with them."""
+    q = _lib.GemmParams()
+    q.m, q.n, q.k, q.r = 512, 512, 1024, 128
+    for i, (name, _) in enumerate(_lib.GemmParams._fields_):
+        if name in ("AxEBL_int32", "EARxBpEB_int32", "host_signal_header_pinned", "inner_hash_counter",
+                    "hits", "transcripts", "digests"):
+            continue
+        if _ == ctypes.c_void_p:
+            setattr(q, name, 0x10000 * (i + 1))
+    q.tile_size_m, q.tile_size_n, q.tile_size_k = 128, 256, 128
+    q.cluster_size_m = q.cluster_size_n = 1
+    q.run_noising_a = q.run_noising_b = 1
+    return q
+
+
+@pytest.mark.parametrize("missing", ["A", "EAL", "EAR_R_major", "EBL_K_major", "B", "EBR", "EAR_K_major",
+                                     "EBL_R_major", "ApEA", "C", "A_scales", "host_signal_sync",
+                                     "pow_target", "EAL_fp16", "EARxBpEB_fp16"])
+def test_static_scratch_rejects_missing_operands_before_any_cuda_call(missing):
+    """A call with an absent operand returns PB2_ERR_INVALID_ARGUMENT before
+    it selects the device or clears the shared array (no GPU here: any CUDA
+    call would fail with PB2_ERR_CUDA instead), so a rejected call never
+    disturbs a call still running on the array."""
+    L = _lib.load()
+    q = _complete_params()
+    setattr(q, missing, None)
+    assert L.pb2_noisy_gemm_static_scratch(ctypes.byref(q), None) == _lib.PB2_ERR_INVALID_ARGUMENT
+    assert L.pb2_noisy_gemm(ctypes.byref(q), None) == _lib.PB2_ERR_INVALID_ARGUMENT
