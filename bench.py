@@ -74,15 +74,15 @@ class BenchProblem:
 def bind_to_gpu_numa_node(dev: torch.device) -> str | None:
     """Restrict this process to the CPUs of the GPU's own NUMA node, so the
     pinned host buffers of the e2e leg (first touched by this process) sit
-    on the node whose PCIe root serves the GPU.  Returns the CPU list used,
-    or None when the topology cannot be read (nothing is changed then)."""
+    on the node whose PCIe root serves the GPU.  Returns the node and CPU
+    list used, or why nothing was changed."""
     try:
         props = torch.cuda.get_device_properties(dev)
         bus = f"{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
         base = f"/sys/bus/pci/devices/{bus}"
         node = int(open(f"{base}/numa_node").read().strip())
         if node < 0:
-            return None
+            return f"none: {bus} reports no NUMA node"
         cpulist = open(f"/sys/devices/system/node/node{node}/cpulist").read().strip()
         cpus = set()
         for part in cpulist.split(","):
@@ -90,8 +90,8 @@ def bind_to_gpu_numa_node(dev: torch.device) -> str | None:
             cpus.update(range(int(lo), int(hi or lo) + 1))
         os.sched_setaffinity(0, cpus)
         return f"node {node}: {cpulist}"
-    except (AttributeError, OSError, ValueError):
-        return None
+    except (AttributeError, OSError, ValueError) as e:
+        return f"none: {type(e).__name__}: {e}"
 
 
 def signal_buffers(pg, device):

@@ -8,9 +8,8 @@ from __future__ import annotations
 import ctypes
 import enum
 import logging
-from collections import deque
 from dataclasses import dataclass
-from threading import Lock, Semaphore
+from threading import Lock
 
 import torch
 
@@ -107,37 +106,49 @@ def get_host_signal_sync_fields(host_signal_sync: torch.Tensor) -> dict:
 
 
 class HostSignalHeaderPinnedPool:
-    """Thread-safe pool of pinned header buffers (helpers.py:27-65)."""
+    """Pinned host-signal headers for concurrent mined GEMMs, with the
+    reference pool's interface (helpers.py:27-65): ``acquire()`` hands out a
+    zeroed 640-byte pinned int8 header and blocks while all ``pool_size``
+    are out; ``release(buffer)`` zeroes it and returns it; both are safe to
+    call from several threads.
+
+    The headers are slots of ONE pinned allocation made up front (one
+    page-locked region instead of ``pool_size`` small ones); the free slots
+    wait in a blocking FIFO queue, and a released tensor is matched to its
+    slot by its address, so a tensor that is not a slot of this pool, or a
+    slot released twice, is refused with ValueError."""
 
     def __init__(self, pool_size: int = 128) -> None:
+        import queue
+
+        if pool_size <= 0:
+            raise ValueError("pool_size must be positive")
         self._pool_size = pool_size
-        self._available_buffers = deque()
-        self._used_buffers: set[int] = set()
-        self._lock = Lock()
-        self._semaphore = Semaphore(self._pool_size)
         size = get_host_signal_header_size()
-        for _ in range(self._pool_size):
-            self._available_buffers.append(torch.zeros((size,), dtype=torch.int8, pin_memory=True))
+        self._slab = torch.zeros((pool_size, size), dtype=torch.int8, pin_memory=True)
+        self._slot_of = {int(self._slab[i].data_ptr()): i for i in range(pool_size)}
+        self._out: set[int] = set()
+        self._out_lock = Lock()
+        self._free: "queue.Queue[int]" = queue.Queue()
+        for i in range(pool_size):
+            self._free.put(i)
 
     def acquire(self) -> torch.Tensor:
-        if not self._available_buffers:
-            _LOG.warning("Pool size exceeded, self._pool_size=%d", self._pool_size)
-        self._semaphore.acquire()
-        with self._lock:
-            buffer = self._available_buffers.popleft()
-            if id(buffer) in self._used_buffers:
-                raise AssertionError("Unexpectedly found available buffer in _used_buffers")
-            self._used_buffers.add(id(buffer))
-            return buffer
+        if self._free.empty():
+            _LOG.warning("all %d pinned headers are in use; waiting for a release", self._pool_size)
+        slot = self._free.get()  # blocks until a header comes back
+        with self._out_lock:
+            self._out.add(slot)
+        return self._slab[slot]
 
     def release(self, buffer: torch.Tensor) -> None:
-        with self._lock:
-            if id(buffer) not in self._used_buffers:
-                raise ValueError("Attempted to release unused buffer")
-            self._used_buffers.remove(id(buffer))
-            self._available_buffers.append(buffer)
-            buffer.zero_()
-        self._semaphore.release()
+        slot = self._slot_of.get(int(buffer.data_ptr())) if buffer.numel() == self._slab.shape[1] else None
+        with self._out_lock:
+            if slot is None or slot not in self._out:
+                raise ValueError("release() got a header this pool has not handed out")
+            self._out.discard(slot)
+        self._slab[slot].zero_()
+        self._free.put(slot)
 
 
 @dataclass

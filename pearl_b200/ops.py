@@ -108,11 +108,12 @@ _UNTAGGED = ("inner_hash", "tensor_hash", "commitment_hash_from_merkle_roots", "
 
 _TAGS = (torch.Tag.pt2_compliant_tag,)
 _lib = None
+_fake_lib = None
 REGISTERED = False
 
 
 def _register() -> None:
-    global _lib, REGISTERED
+    global _lib, _fake_lib, REGISTERED
     try:
         lib = torch.library.Library("pearl_gemm", "DEF")
     except RuntimeError as e:  # namespace already owned (e.g. the reference extension)
@@ -121,14 +122,30 @@ def _register() -> None:
     for name, schema in SCHEMAS.items():
         lib.define(schema, tags=() if name in _UNTAGGED else _TAGS)
         lib.impl(name, _IMPLS[name], "CUDA")
+    # The fake implementations live in a library object of their own, so
+    # that release_fake_impls() can hand them over to the reference's
+    # interface files (which register theirs at import).
+    fake = torch.library.Library("pearl_gemm", "FRAGMENT")
     for name in SCHEMAS:
         if name == "inner_hash":
-            torch.library.register_fake(f"pearl_gemm::{name}", lib=lib)(
+            torch.library.register_fake(f"pearl_gemm::{name}", lib=fake)(
                 lambda input_buffer, iterations=1: input_buffer.new_empty((1,)))
         else:
-            torch.library.register_fake(f"pearl_gemm::{name}", lib=lib)(lambda *a, **k: None)
-    _lib = lib
+            torch.library.register_fake(f"pearl_gemm::{name}", lib=fake)(lambda *a, **k: None)
+    _lib, _fake_lib = lib, fake
     REGISTERED = True
+
+
+def release_fake_impls() -> None:
+    """Withdraw pearl_b200's fake implementations of torch.ops.pearl_gemm.*,
+    leaving the schemas and CUDA implementations.  The reference's extension
+    defines the ops and its Python files (pearl_gemm_interface.py:36-628,
+    moe.py:34) register the fakes; running that package on these kernels
+    (through pearl_b200.pearl_gemm_cuda) needs the same split."""
+    global _fake_lib
+    if _fake_lib is not None:
+        _fake_lib._destroy()
+        _fake_lib = None
 
 
 _register()

@@ -3,7 +3,9 @@ own part of the nonce space, with no collective on the data path.
 
 Every hash tile of every mined GEMM is independent and the noise is a
 function of the GEMM's own commitment, so ranks never exchange operands: a
-rank mines GEMMs whose seeds (job keys) no other rank uses.  What crosses
+rank mines GEMMs whose seeds (job keys) no other rank uses -- in production
+because every rank mines a block header of its own (job_key), in the
+benchmark through synthetic per-rank keys (rank_job_key).  What crosses
 ranks is only what the host needs afterwards -- the winning proofs, a few
 hundred bytes each at ~1e-6 hits per hash tile -- gathered to rank 0 after
 the work, and the elapsed time, reduced to the maximum over ranks.  The
@@ -19,9 +21,29 @@ import torch
 HIT_WORDS = 12  # {row_offset, col_offset, tile_m, tile_n, digest[8]}
 
 
+def job_key(incomplete_header_bytes: bytes, mining_config_bytes: bytes) -> bytes:
+    """The protocol's commitment key of a mining job: BLAKE3 of the
+    incomplete block header followed by the serialized mining configuration
+    (miner-base commitment_hash.py:36-37, CommitmentHasher.get_key).
+
+    This is how a rank's real work is kept apart from every other rank's:
+    each rank mines a header of its own (the coinbase extranonce, and so the
+    header's merkle root, differs per rank), so its key, its noise seeds and
+    every hash tile it hashes are its own, and a verifier derives the same
+    key from the submitted header."""
+    from blake3 import blake3
+
+    return blake3(bytes(incomplete_header_bytes) + bytes(mining_config_bytes)).digest()
+
+
 def rank_job_key(base_key: bytes, rank: int, step: int) -> bytes:
-    """32-byte job key of GEMM `step` on `rank`: distinct for every (rank,
-    step), so no two ranks ever mine the same noise."""
+    """Benchmark stand-in for job_key: a 32-byte key distinct for every
+    (rank, step), so no two ranks of a benchmark mine the same noise.
+
+    These keys come from no block header, so a verifier could not rebuild
+    them and proofs mined with them would not validate; they only give the
+    benchmark independent work per rank without a gateway.  Real mining
+    derives each rank's key with job_key from the header that rank mines."""
     h = hashlib.blake2b(digest_size=32, key=base_key[:64])
     h.update(rank.to_bytes(4, "little") + step.to_bytes(8, "little"))
     return h.digest()

@@ -317,3 +317,44 @@ def test_inner_hash_op():
         want ^= v
     assert int(pg.inner_hash(x, 1).item()) == want
     assert int(pg.inner_hash(x, 100000).item()) == (want * 100000) % 2 ** 32
+
+
+def test_pearl_gemm_cuda_positional_calls():
+    """The extension-module surface (pearl_b200.pearl_gemm_cuda) called the
+    way the reference's pearl_gemm_interface.py calls its compiled extension:
+    every argument positional, in the C++ order (pearl_gemm_api.cpp:168,
+    618-656, 502-510).  Noise, noised operands and the hit set against the
+    oracle, C within the reference tolerance."""
+    from pearl_b200 import pearl_gemm_cuda as ext
+
+    m, n, k, r = 256, 512, 1024, 128
+    p = make_problem(m, n, k, r, seed=91)
+    nz = p.noise
+    ext.noise_gen(r, 64, nz["EAL"], nz["EAL_fp16"], nz["EAR_R_major"], nz["EAR_K_major"], nz["EBL_R_major"],
+                  nz["EBL_K_major"], nz["EBR"], nz["EBR_fp16"], p.key_a, p.key_b, None)
+    o = oracle_problem(p)
+    assert np.array_equal(_np(nz["EAL"]), o.EAL) and np.array_equal(_np(nz["EBR"]), o.EBR)
+    ref = O.mine_tiles(o.ApEA, o.BpEB, r, _np(p.key_a).tobytes(), 0)
+    target = _target_for_fraction(ref.digests, 0.01)
+    want = O.hit_set(O.mine_tiles(o.ApEA, o.BpEB, r, _np(p.key_a).tobytes(), target), m, n)
+    header = torch.zeros(ext.get_host_signal_header_size(), dtype=torch.int8, pin_memory=True)
+    sync = torch.zeros(ext.get_host_signal_sync_size(), dtype=torch.int8, device="cuda")
+    out = p.out
+    ext.noisy_gemm(p.A, p.B, nz["EAL"], nz["EAL_fp16"], nz["EBR"], nz["EBR_fp16"], nz["EAR_R_major"],
+                   nz["EBL_R_major"], nz["EAR_K_major"], nz["EBL_K_major"], out["AxEBL_fp16"],
+                   out["EARxBpEB_fp16"], out["ApEA"], out["BpEB"], p.A_scales, p.B_scales, out["C"], header, sync,
+                   pg.make_pow_target_tensor(target), p.key_a.view(torch.uint32), None, None, 128, 256, 128, 1, 1,
+                   None, None, True, None, None, None, None, 2, 2, None, None, True, True, False, False, None,
+                   False)
+    torch.cuda.synchronize()
+    assert np.array_equal(_np(out["ApEA"]), o.ApEA) and np.array_equal(_np(out["BpEB"]), o.BpEB)
+    f = pg.get_host_signal_sync_fields(sync)
+    assert f["error"] == 0 and f["hit_count"] == len(want) and f["status"] == 1
+    hdr = ext.get_host_signal_header(header)
+    assert hdr.status == ext.HostSignalStatus.kSignalTriggered
+    idx = pg.extract_indices(hdr)
+    assert (idx.A_row_indices[0], idx.B_column_indices[0]) in want
+    torch.testing.assert_close(out["C"].float().cpu(), ref_c(p).to(torch.bfloat16).float(), atol=ATOL, rtol=RTOL)
+    C2 = torch.empty_like(out["C"])
+    ext.gemm(p.A, p.B, p.A_scales, p.B_scales, C2, 128, 256, 128, 1, 1, None, None, True)
+    torch.testing.assert_close(C2.float().cpu(), ref_c(p).to(torch.bfloat16).float(), atol=ATOL, rtol=RTOL)

@@ -273,3 +273,32 @@ def test_scatter_rows_matches_index_put():
     want2 = torch.zeros_like(want)
     want2[perm[keep].long()] = src[keep]
     assert torch.equal(got2, want2)
+
+
+# --------------------------------------------------------- pinned pool ---
+def test_pinned_header_pool_contract():
+    """acquire() hands out zeroed, distinct, 128-byte aligned pinned
+    headers and blocks when all are out; release() zeroes a header and
+    refuses one the pool did not hand out or that is already back."""
+    import threading
+
+    pool = pg.HostSignalHeaderPinnedPool(pool_size=3)
+    bufs = [pool.acquire() for _ in range(3)]
+    assert len({b.data_ptr() for b in bufs}) == 3
+    for b in bufs:
+        assert b.is_pinned() and b.dtype == torch.int8 and b.numel() == pg.get_host_signal_header_size()
+        assert b.data_ptr() % 128 == 0 and int(b.abs().sum()) == 0
+    bufs[0].fill_(7)
+    got = []
+    t = threading.Thread(target=lambda: got.append(pool.acquire()))
+    t.start()
+    t.join(0.2)
+    assert t.is_alive() and not got  # every header is out: acquire waits
+    pool.release(bufs[0])
+    t.join(5)
+    assert got and got[0].data_ptr() == bufs[0].data_ptr() and int(got[0].abs().sum()) == 0
+    with pytest.raises(ValueError):
+        pool.release(torch.zeros(pg.get_host_signal_header_size(), dtype=torch.int8, pin_memory=True))
+    pool.release(bufs[1])
+    with pytest.raises(ValueError):
+        pool.release(bufs[1])

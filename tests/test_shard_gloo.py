@@ -103,3 +103,16 @@ def test_dead_rank_fails_the_gather_instead_of_hanging():
             pytest.fail("a rank hung")
     assert res[1] == "left"
     assert res[0].startswith("error"), res[0]
+
+
+def test_job_key_is_the_protocol_key():
+    """A rank's real key is BLAKE3(incomplete header || mining config)
+    (commitment_hash.py:36-37); ranks mining different headers (their own
+    extranonce) get different keys."""
+    from oracle import oracle as O
+
+    header = bytes(range(80))
+    config = bytes([3, 0, 0, 0, 128, 0, 0, 0])
+    assert shard.job_key(header, config) == O.blake3(header + config)
+    other = header[:-4] + (1).to_bytes(4, "little")
+    assert shard.job_key(other, config) != shard.job_key(header, config)
