@@ -247,8 +247,10 @@ def run_ours(args, world, rank, local):
         total_hits = None if gathered is None else int(gathered.shape[0])
 
     # ---- end to end through the public API with host buffers -------------
-    e2e = run_e2e(args, p, keys_a, keys_b, target, header, sync, dev, world)
-    e2e["host_numa_binding"] = numa
+    e2e = None
+    if args.e2e_steps > 0:
+        e2e = run_e2e(args, p, keys_a, keys_b, target, header, sync, dev, world)
+        e2e["host_numa_binding"] = numa
     os.sched_setaffinity(0, all_cpus)  # the CPU baseline below uses every host core
 
     # ---- live cuBLAS int8 reference point (rank 0) ------------------------
@@ -294,7 +296,8 @@ def run_ours(args, world, rank, local):
         "vs_baseline": None,
         "dtype": "int8",
         "data": "synthetic (seeded int7 operands, fresh noise seeds per step)",
-        "config": {"workload": "pearl-gemm noisy_gemm M=N=K=8192 R=128, target 1e-6 hits/hash tile",
+        "config": {"workload": (f"pearl-gemm noisy_gemm M=N={M} K={K} R=128, target 1e-6 hits/hash tile"
+                                if K != 8192 else "pearl-gemm noisy_gemm M=N=K=8192 R=128, target 1e-6 hits/hash tile"),
                    "m": M, "n": N, "k": K, "r": R, "hash_tile": "2x64",
                    "l2": "inputs larger than L2: A,B,ApEA,BpEB,C = 384 MiB per step > 126 MB",
                    "parallelism": f"nonce-space shards x{world}"},
@@ -322,7 +325,8 @@ def run_ours(args, world, rank, local):
     }
     # The CPU baseline is timed at N = 1 only: under torchrun the host cores
     # are shared by every rank's process.
-    line["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget) if world == 1 else None
+    line["cpu_baseline"] = (cpu_baseline(budget_s=args.cpu_budget)
+                            if world == 1 and args.cpu_budget > 0 and K == 8192 else None)
     return line
 
 
@@ -635,7 +639,12 @@ def main():
                     choices=["gemm8192", "gemm16384", "llama", "llama_decode", "moe"],
                     help="gemm8192 (default) is the headline GEMM; the others are the larger "
                          "configs 3-5 measured through the miner-facing operators")
+    ap.add_argument("--k", type=int, default=8192,
+                    help="K of the default GEMM workload (8192 is the headline; a smaller K gives the "
+                         "small case the full ncu sections are captured on)")
     args = ap.parse_args()
+    global K
+    K = args.k
     if args.warmup < 3:
         args.warmup = 3
     world, rank, local = setup_dist(args)

@@ -366,10 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
           tc_fence_after();
           const uint64_t ad = sdesc_kmajor<BK>(sbase + j * kStageBytes);
           const uint64_t bd = sdesc_kmajor<BK>(sbase + j * kStageBytes + kAStage);
-          umma_i8_2sm_warp(dt, ad, bd, kIdescI8, uint32_t((u | st) != 0));
-#pragma unroll
-          for (int ks = 1; ks < BK / 32; ++ks) umma_i8_2sm_warp(dt, ad + 2 * ks, bd + 2 * ks, kIdescI8, 1);
-          umma_commit_2sm_warp(&S.empty[j], kPairMask);
+          umma_i8_2sm_stage_warp<BK / 32>(dt, ad, bd, kIdescI8, uint32_t((u | st) != 0), &S.empty[j], kPairMask);
         }
         // With the transcript every unit is a fold event, and the stage's
         // commit above doubles as "accumulator ready" (one commit per unit

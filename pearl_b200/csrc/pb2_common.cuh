@@ -87,6 +87,24 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: while the phase is incomplete the warp
+// is suspended in hardware (up to kSuspendNs) and resumes when the phase
+// completes, instead of spinning.  A spinning waiter takes issue slots from
+// the warps it waits for when they share its sub-partition: the MMA issuer
+// waiting for a slot release starved the fold warps on its own
+// sub-partition, which held the release back by ~1500 cycles per R-chunk.
+constexpr uint32_t kSuspendNs = 1000000;
+__device__ __forceinline__ bool mbar_test_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait for the phase with the given parity.  Returns false (and
 // records the error / raises the CTA abort flag) if the budget runs out or
 // another warp of the CTA already aborted.
@@ -95,7 +113,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (mbar_test(bar, parity)) return true;
   long long t0 = clock64();
   while (true) {
-    if (mbar_test(bar, parity)) return true;
+    if (mbar_test_suspend(bar, parity)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > budget) {
       *abort_flag = 1;
@@ -113,16 +131,14 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, v
   return __all_sync(0xffffffffu, ok);
 }
 
-// Bounded wait for warps that may idle a long time (no spin on the barrier
-// between polls, so the polling does not compete for issue slots and the
-// shared-memory pipe with latency-critical warps).
+// Bounded wait for warps that may idle a long time (the same suspending
+// wait; kept as its own name for the warps whose waits are long by design).
 __device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                                SignalSync* sync, long long budget = kWaitBudgetCycles) {
   if (mbar_test(bar, parity)) return true;
   long long t0 = clock64();
   while (true) {
-    __nanosleep(100);
-    if (mbar_test(bar, parity)) return true;
+    if (mbar_test_suspend(bar, parity)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > budget) {
       *abort_flag = 1;
@@ -441,6 +457,48 @@ __device__ __forceinline__ void umma_commit_2sm_warp(uint64_t* bar, uint16_t cta
       " [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
       "h"(cta_mask)
       : "memory");
+}
+
+// One operand stage of 2-SM i8 MMAs and the stage's commit from ONE elected
+// lane: kSteps MMAs along K (32 bytes each; the first accumulates only if
+// `accumulate`), then a commit of all of them to `bar` in every CTA of
+// `cta_mask`.  One election and one predicated block per stage keep the
+// issuing warp's instruction count low; it shares its sub-partition (and
+// that sub-partition's tcgen05 instruction path) with fold warps.
+template <int kSteps>
+__device__ __forceinline__ void umma_i8_2sm_stage_warp(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                                       uint32_t idesc, uint32_t accumulate, uint64_t* bar,
+                                                       uint16_t cta_mask) {
+  static_assert(kSteps == 2 || kSteps == 4, "K steps per stage");
+  if constexpr (kSteps == 4) {
+    asm volatile(
+        "{\n\t.reg .pred e, p;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t"
+        "setp.eq.u32 p, %4, %4;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::i8 [%0], %5, %6, %3, p;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::i8 [%0], %7, %8, %3, p;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::i8 [%0], %9, %10, %3, p;\n\t"
+        "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+        " [%11], %12;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "l"(adesc + 2), "l"(bdesc + 2), "l"(adesc + 4),
+        "l"(bdesc + 4), "l"(adesc + 6), "l"(bdesc + 6), "r"(smem_u32(bar)), "h"(cta_mask)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred e, p;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t"
+        "setp.eq.u32 p, %4, %4;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::i8 [%0], %5, %6, %3, p;\n\t"
+        "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+        " [%7], %8;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "l"(adesc + 2), "l"(bdesc + 2),
+        "r"(smem_u32(bar)), "h"(cta_mask)
+        : "memory");
+  }
 }
 
 // 2-D tiled load into this CTA's shared memory whose transaction bytes are
