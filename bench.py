@@ -569,7 +569,7 @@ def run_workload(args, world, rank, local):
             if len(done) > 8:
                 MN.release_header(done.pop(0).host_signal_header_pinned)
         ms = _time_steps(step, args.steps, args.warmup, dev, world)
-        return _line(args, world, "config 3 shape, int8 path: noisy GEMM M=16384 N=K=8192 with "
+        return _line(args, world, "16384 x 8192 x 8192 int8 mined GEMM with "
                      "commitment (tensor_hash A,B), noise_gen, noising, transcript, BLAKE3",
                      2.0 * m * n * k, ms, {"m": m, "n": n, "k": k, "r": R}, 1) if rank == 0 else None
     if args.workload in ("llama", "llama_decode"):
@@ -598,13 +598,41 @@ def run_workload(args, world, rank, local):
             for mnd in lin.mined:
                 MN.release_header(mnd.host_signal_header_pinned)
             lin.mined.clear()
+        graphed = False
+        if tokens < 1024:
+            # The decode step runs as one CUDA graph, as vLLM runs its decode
+            # batches: 128 quantize + GEMM pairs would otherwise be launched
+            # from Python one by one, and the GPU would wait on the host.
+            for i in range(2):
+                step(i)
+            torch.cuda.synchronize(dev)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                step(0)
+            step = lambda i: graph.replay()  # noqa: E731
+            graphed = True
         ms = _time_steps(step, args.steps, args.warmup, dev, world)
         ops = layers * sum(2.0 * tokens * n_out * k_in for _, n_out, k_in in shapes)
         mined = layers * len(shapes) if tokens >= 1024 else 0
-        return _line(args, world, f"config 4: Llama-3-8B linear layers x32 through PearlLinear.apply_weights "
+        if rank != 0:
+            return None
+        line = _line(args, world, f"Llama-3-8B linear layers x32 through PearlLinear.apply_weights "
                      f"({tokens} tokens: {'mined' if mined else 'vanilla int8'} branch, int7 quantization "
                      f"included)", ops, ms, {"tokens": tokens, "hidden": hidden, "mlp": mlp,
-                                             "layers": layers}, mined) if rank == 0 else None
+                                             "layers": layers, "cuda_graph": graphed}, mined)
+        if not mined:
+            # The decode step streams every weight once per layer: 218 MB of
+            # int8 weights per layer (more than the 126 MB L2, so each GEMM
+            # reads its weight from HBM even though the synthetic layers
+            # share one weight per projection).
+            wbytes = layers * sum(n_out * k_in for _, n_out, k_in in shapes)
+            peak = measured_peaks()["hbm_gbs"]
+            achieved = wbytes / (ms * 1e-3) / 1e9
+            line["roofline"] = {"kernel": "whole decode step (weight streaming)", "bound": "hbm",
+                                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                                "frac": round(achieved / peak, 4), "traffic": None,
+                                "algorithmic_bytes_per_step": wbytes}
+        return line
     if args.workload == "moe":
         E, tokens, top_k, N, K = 8, 16384, 2, 2 * 14336, 4096
         A = torch.randint(-64, 64, (tokens, K), generator=g, dtype=torch.int8).to(dev)
@@ -619,7 +647,7 @@ def run_workload(args, world, rank, local):
             for mnd in res.per_expert.values():
                 MN.release_header(mnd.host_signal_header_pinned)
         ms = _time_steps(step, args.steps, args.warmup, dev, world)
-        return _line(args, world, "config 5: Mixtral-8x7B MoE GEMM1 (8 experts, 16384 tokens, top-2, "
+        return _line(args, world, "Mixtral-8x7B MoE GEMM1 (8 experts, 16384 tokens, top-2, "
                      "N=2x14336, K=4096), routing + commitment + one mined GEMM per expert",
                      2.0 * tokens * top_k * N * K, ms, {"experts": E, "tokens": tokens, "top_k": top_k,
                                                          "n": N, "k": K}, E) if rank == 0 else None

@@ -64,6 +64,7 @@ struct MainArgs {
   CUtensorMap tmC;           // C (m,n) bf16, 32 x 32 boxes, 64-byte swizzle
   int M, N, K, R;
   int tiles_m, tiles_n, num_tiles, group;
+  int tpr;  // tiles a CTA pair runs per round: 2 (two TMEM slots in alternation) or 1
   const float* sA;
   const float* sB;
   __nv_bfloat16* C;
@@ -180,17 +181,23 @@ __device__ void publish_hit(const MainArgs& a, int tm128, int tn, int row_in_til
 // keeps the per-unit bookkeeping of the producer, issuer and fold warps free
 // of runtime loops and divisions (measured: several hundred cycles per unit
 // on the issuer otherwise).
-template <int BK, int kSPU, bool kReduce, bool kDenoise, bool kDebug>
+//
+// kTN = tile width: 256, or 128 for the plain GEMM of small problems (fewer
+// than two 256-wide tiles per SM pair: a decode batch), where narrower tiles
+// put more of the 148 SMs to work; the transcript and denoise variants
+// always use 256 (the hash-tile column period).
+template <int BK, int kSPU, bool kReduce, bool kDenoise, bool kDebug, int kTN>
 __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_constant__ MainArgs a) {
+  static_assert(kTN == BN || (kTN == BN / 2 && !kReduce && !kDenoise), "narrow tiles: plain GEMM only");
   constexpr int kAStage = BMC * BK;        // this CTA's 128 rows of A
-  constexpr int kBStage = (BN / 2) * BK;   // this CTA's half of the 256 rows of B
+  constexpr int kBStage = (kTN / 2) * BK;  // this CTA's half of the tile's rows of B
   constexpr int kStageBytes = kAStage + kBStage;
   constexpr int kStageBudget = stage_budget(kReduce);
   constexpr int kStages =
       (kStageBudget / kStageBytes) < kMaxStages ? (kStageBudget / kStageBytes) : kMaxStages;
   static_assert(kStageBudget + (kReduce ? kXbufBytes : 0) + kCStageBytes + 1024 + 256 <= 232448,
                 "shared memory plan exceeds 227 KB");
-  constexpr uint32_t kIdescI8 = idesc_i8(BM, BN);
+  constexpr uint32_t kIdescI8 = idesc_i8(BM, kTN);
   constexpr uint32_t kIdescF16 = idesc_f16(BM, BN);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -257,10 +264,11 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
   const uint32_t tmem = S.tmem_base;
 
   // Pair tiles are processed in rounds: round r holds tiles t0 = first + r *
-  // stride (slot 0) and t0 + 1 (slot 1, when it exists); within a round the
-  // units alternate slot 0, slot 1.  Every role walks this order.
-  const int first = 2 * int(blockIdx.x >> 1);
-  const int stride = int(gridDim.x);
+  // stride (slot 0) and t0 + 1 (slot 1, when it exists and a.tpr == 2);
+  // within a round the units alternate slot 0, slot 1.  Every role walks
+  // this order.
+  const int first = a.tpr * int(blockIdx.x >> 1);
+  const int stride = a.tpr * int(gridDim.x >> 1);
   using I0 = std::integral_constant<int, 0>;
   using I1 = std::integral_constant<int, 1>;
 
@@ -273,13 +281,13 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
       uint32_t it = 0;
       bool ok = true;
       for (int t0 = first; t0 < a.num_tiles && ok; t0 += stride) {
-        const bool two = t0 + 1 < a.num_tiles;
+        const bool two = a.tpr == 2 && t0 + 1 < a.num_tiles;
         int tm0, tn0, tm1 = 0, tn1 = 0;
         tile_coords(a, t0, tm0, tn0);
         if (two) tile_coords(a, t0 + 1, tm1, tn1);
         // This CTA's 128 rows of A and half of the B rows, per slot.
-        const int ma = tm0 * BM + int(rank) * BMC, na = tn0 * BN + int(rank) * (BN / 2);
-        const int mb = tm1 * BM + int(rank) * BMC, nb = tn1 * BN + int(rank) * (BN / 2);
+        const int ma = tm0 * BM + int(rank) * BMC, na = tn0 * kTN + int(rank) * (kTN / 2);
+        const int mb = tm1 * BM + int(rank) * BMC, nb = tn1 * kTN + int(rank) * (kTN / 2);
         // Main units, then the denoise units, in the issuer's order.  The two
         // loops are kept apart (and the tensor maps named, not selected), so
         // the per-stage code on the main path stays minimal.
@@ -393,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
         }
       };
       for (int t0 = first; t0 < a.num_tiles && ok; t0 += stride) {
-        const bool two = t0 + 1 < a.num_tiles;
+        const bool two = a.tpr == 2 && t0 + 1 < a.num_tiles;
         for (int u = 0; u < nmain && ok; ++u) {
           main_unit(0, u);
           if (two && ok) main_unit(1, u);
@@ -555,14 +563,17 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
       if (do_store) {  // scales first: their latency overlaps the loads
         const int row = tm * BM + int(rank) * BMC + 32 * q + lane;
         rs = (row < a.M ? a.sA[row] : 0.0f) * (is_main ? 1.0f : 4096.0f);
-        const int c = tn * BN + 64 * wi + 2 * lane;  // this lane's two column scales
+        const int c = tn * kTN + 64 * wi + 2 * lane;  // this lane's two column scales
         if (c < a.N) sbv = *reinterpret_cast<const float2*>(a.sB + c);
       }
       const int row0 = tm * BM + int(rank) * BMC + 32 * q;
       uint8_t* box = cstage + fw * kCBoxBytes;
       uint32_t p0 = 0, p1 = 0, p2 = 0, p3 = 0;
+      // With 128-wide tiles the strips beyond the tile hold nothing to store.
+      const bool strip_live = 64 * wi < kTN;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
+        if (!strip_live) break;
         uint32_t v[32];
         __syncwarp();
         tmem_ld32(taddr + 32 * h, v);
@@ -585,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
             const float f1 = is_main ? float(int(v[i + 1])) : __uint_as_float(v[i + 1]);
             packed[i / 2] = pack_bf16(f0 * rs * bx, f1 * rs * by);
           }
-          store_c_packed(a, box, packed, row0, tn * BN + 64 * wi + 32 * h, lane);
+          store_c_packed(a, box, packed, row0, tn * kTN + 64 * wi + 32 * h, lane);
         }
       }
       if (do_convert) tmem_wait_st();
@@ -595,7 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
 
     uint32_t it = 0;  // operand stages issued so far, in the issuer's order
     for (int t0 = first; t0 < a.num_tiles && ok; t0 += stride) {
-      const bool two = t0 + 1 < a.num_tiles;
+      const bool two = a.tpr == 2 && t0 + 1 < a.num_tiles;
       int tm0, tn0, tm1 = 0, tn1 = 0;
       tile_coords(a, t0, tm0, tn0);
       if (two) tile_coords(a, t0 + 1, tm1, tn1);
@@ -654,7 +665,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
       if (lane == 0) mbar_arrive(&S.xfree[b]);
     };
     for (int t0 = first; t0 < a.num_tiles && ok; t0 += stride) {
-      const bool two = t0 + 1 < a.num_tiles;
+      const bool two = a.tpr == 2 && t0 + 1 < a.num_tiles;
       const int round = (t0 - first) / stride;
       int tm0, tn0, tm1 = 0, tn1 = 0;
       tile_coords(a, t0, tm0, tn0);
@@ -676,9 +687,16 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
 }
 
 // ------------------------------------------------------------------ host
-template <int BK, int SPU, bool R_, bool D_, bool G_>
+// CTA pairs of the mined-GEMM kernels resident at once on `device` (SM pairs
+// in one GPC; 0 until the first launch there has asked the occupancy API).
+int& resident_pairs(int device) {
+  static int cached[64] = {0};
+  return cached[device & 63];
+}
+
+template <int BK, int SPU, bool R_, bool D_, bool G_, int TN = BN>
 int launch_variant(const MainArgs& a, int device, cudaStream_t s) {
-  auto kern = noisy_gemm_kernel<BK, SPU, R_, D_, G_>;
+  auto kern = noisy_gemm_kernel<BK, SPU, R_, D_, G_, TN>;
   const int smem = stage_budget(R_) + (R_ ? kXbufBytes : 0) + kCStageBytes + int(sizeof(Smem)) + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return launch_status();
@@ -695,8 +713,7 @@ int launch_variant(const MainArgs& a, int device, cudaStream_t s) {
   cfg.numAttrs = 1;
   // A persistent grid: as many CTA pairs as can be co-resident (SM pairs in
   // one GPC), never more than half the tiles (each pair runs two slots).
-  static int cached_pairs[64] = {0};
-  int& resident = cached_pairs[device & 63];
+  int resident = resident_pairs(device);
   if (resident == 0) {
     cfg.gridDim = dim3(2, 1, 1);
     int clusters = 0;
@@ -706,8 +723,9 @@ int launch_variant(const MainArgs& a, int device, cudaStream_t s) {
       clusters = (sms > 0 ? sms : 148) / 2;
     }
     resident = clusters;
+    resident_pairs(device) = clusters;
   }
-  const int pairs = std::max(1, std::min((a.num_tiles + 1) / 2, resident));
+  const int pairs = std::max(1, std::min((a.num_tiles + a.tpr - 1) / a.tpr, resident));
   cfg.gridDim = dim3(unsigned(2 * pairs), 1, 1);
   cudaLaunchAttribute attrs[2] = {attr[0], {}};
   attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see griddep_wait
@@ -719,7 +737,9 @@ int launch_variant(const MainArgs& a, int device, cudaStream_t s) {
 }
 
 template <int BK, int SPU>
-int launch_spu(const MainArgs& a, int device, bool reduce, bool denoise, bool debug, cudaStream_t s) {
+int launch_spu(const MainArgs& a, int device, bool reduce, bool denoise, bool debug, bool narrow,
+               cudaStream_t s) {
+  if (narrow) return launch_variant<BK, SPU, false, false, false, BN / 2>(a, device, s);
   if (reduce && denoise) return debug ? launch_variant<BK, SPU, true, true, true>(a, device, s)
                                       : launch_variant<BK, SPU, true, true, false>(a, device, s);
   if (reduce) return debug ? launch_variant<BK, SPU, true, false, true>(a, device, s)
@@ -768,13 +788,20 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
   // 128-byte stages (128-byte swizzle) unless R = 64, where 64-byte stages
   // (64-byte swizzle) keep a transcript chunk a whole number of stages.
   const int bk = ((reduce || denoise) && p.r == 64) ? 64 : 128;
+  // The plain GEMM of a small problem (fewer than two 256-wide tiles per SM
+  // pair, e.g. a decode batch) runs 128-wide tiles, one per pair and round
+  // while they do not fill the pairs: more SMs streaming the weights.
+  const int64_t tiles_m = (p.m + BM - 1) / BM;
+  const int pairs_est = resident_pairs(p.device) ? resident_pairs(p.device) : std::max(1, sm_count(p.device) / 2);
+  const bool narrow = !reduce && !denoise && tiles_m * ((p.n + BN - 1) / BN) < 2 * int64_t(pairs_est);
+  const int tn_width = narrow ? BN / 2 : BN;
   const CUtensorMapSwizzle swz = bk == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   MainArgs a;
   std::memset(&a, 0, sizeof(a));
   int st;
   if ((st = make_tmap_2d(&a.tmA, p.ApEA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.k, p.m, bk, BMC, swz)))
     return st;
-  if ((st = make_tmap_2d(&a.tmB, p.BpEB, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.k, p.n, bk, BN / 2, swz)))
+  if ((st = make_tmap_2d(&a.tmB, p.BpEB, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.k, p.n, bk, tn_width / 2, swz)))
     return st;
   if ((st = make_tmap_2d(&a.tmC, p.C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.n, p.m, 32, 32,
                          CU_TENSOR_MAP_SWIZZLE_64B)))
@@ -793,8 +820,9 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
   a.K = int(p.k);
   a.R = int(p.r);
   a.tiles_m = int((p.m + BM - 1) / BM);
-  a.tiles_n = int((p.n + BN - 1) / BN);
+  a.tiles_n = int((p.n + tn_width - 1) / tn_width);
   a.num_tiles = a.tiles_m * a.tiles_n;
+  a.tpr = (narrow && a.num_tiles <= pairs_est) ? 1 : 2;
   a.group = p.swizzle > 0 ? p.swizzle : 8;
   if (a.group > a.tiles_m) a.group = a.tiles_m;
   a.sA = p.A_scales;
@@ -815,9 +843,9 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
   // denoise (R = 64: one 64-byte stage; R = 128: one; R = 256: two), else
   // one 128-byte tile_size_k.
   const int spu = (reduce || denoise) ? int(p.r) / bk : kTileK / bk;
-  if (bk == 64) return launch_spu<64, 1>(a, p.device, reduce, denoise, debug, s);
-  return spu == 2 ? launch_spu<128, 2>(a, p.device, reduce, denoise, debug, s)
-                  : launch_spu<128, 1>(a, p.device, reduce, denoise, debug, s);
+  if (bk == 64) return launch_spu<64, 1>(a, p.device, reduce, denoise, debug, false, s);
+  return spu == 2 ? launch_spu<128, 2>(a, p.device, reduce, denoise, debug, false, s)
+                  : launch_spu<128, 1>(a, p.device, reduce, denoise, debug, narrow, s);
 }
 
 int denoise_convert(const int32_t* in, void* out, int64_t count, float scale, cudaStream_t s);

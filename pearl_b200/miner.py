@@ -21,6 +21,7 @@ the commitment hashes of every mined GEMM (``MinedGemm``)."""
 
 from __future__ import annotations
 
+import weakref
 from collections import OrderedDict
 from dataclasses import dataclass, field
 
@@ -206,6 +207,36 @@ def _tensor_root_async(data_u8: torch.Tensor, key: torch.Tensor):
     return root, done
 
 
+_B_ROOTS: "OrderedDict[tuple, tuple]" = OrderedDict()
+
+
+def weight_root(weight: torch.Tensor, job: MiningJob):
+    """(root, event) of the tensor_hash of a weight under a job's key,
+    hashed once per (weight, job) instead of once per GEMM.
+
+    Within a job the key is fixed and a layer's weight bytes do not change,
+    so the root -- and the commitment seeds built from it -- are the same
+    for every GEMM of that weight: the reference re-hashes B each time
+    (gemm_operators.py:96-100), here the first GEMM hashes it (on the side
+    stream, as _tensor_root_async) and later ones reuse the result.  An
+    entry is keyed by the weight object itself (held weakly, so a new tensor
+    at a recycled address never matches) and by its version counter, which
+    every in-place write to the weight advances."""
+    dev = weight.device
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    k = (id(weight), weight._version, job.hash_key, idx)
+    hit = _B_ROOTS.get(k)
+    if hit is not None and hit[0]() is weight:
+        _B_ROOTS.move_to_end(k)
+        return hit[1], hit[2]
+    key_tensor = _job_tensors(job, dev)[0]
+    root, done = _tensor_root_async(weight.contiguous().view(torch.uint8), key_tensor)
+    _B_ROOTS[k] = (weakref.ref(weight), root, done)
+    while len(_B_ROOTS) > 1024:
+        _B_ROOTS.popitem(last=False)
+    return root, done
+
+
 def pearl_gemm_noisy(a, b, scale_a, scale_b, out_dtype, job: MiningJob,
                      config: MiningConfig = MiningConfig(), *, hits: torch.Tensor | None = None,
                      b_root=None):
@@ -270,9 +301,9 @@ class PearlLinear:
             k, n = x.shape[-1], w_q.shape[0]
             m = x.numel() // k
             noisy = self.config.should_use_noisy_gemm(m, n, k) and self.job is not None
-            # the weight's commitment root does not depend on x: hash it beside the quantization
-            b_root = (_tensor_root_async(w_q.contiguous().view(torch.uint8), _job_tensors(self.job, x.device)[0])
-                      if noisy else None)
+            # the weight's commitment root does not depend on x: hashed once
+            # per (weight, job), beside the quantization
+            b_root = weight_root(w_q, self.job) if noisy else None
             x_q, x_s, _ = quant_7bit(x, smooth_scale=smooth, block_size=block)
             if noisy:
                 C, mined = pearl_gemm_noisy(x_q.contiguous(), w_q.contiguous(), x_s.squeeze(-1),

@@ -283,16 +283,34 @@ def test_inner_hash_counter_formula():
         assert int(counter.item()) == tiles * (k // 128) * (128 // 2) * (256 // 64)
 
 
-def test_gemm_vanilla():
-    g = torch.Generator().manual_seed(8)
-    m, n, k = 1000, 768, 1024
-    A = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int8)
-    B = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8)
-    sa, sb = torch.rand(m, generator=g) / 64, torch.rand(n, generator=g) / 64
+@pytest.mark.parametrize("m,n,k", [
+    (1000, 768, 1024),    # 128-wide tiles, one per SM pair
+    (256, 4096, 4096),    # decode-batch shapes (Llama-3-8B o / qkv / gate_up / down): 128-wide tiles
+    (256, 6144, 4096),
+    (256, 28672, 4096),   # 224 narrow tiles: two per pair and round
+    (256, 4096, 14336),
+    (200, 1000, 384),     # ragged m and n
+    (4096, 8192, 1024)])  # 256-wide tiles, two per pair and round
+def test_gemm_vanilla(m, n, k):
+    """The plain scaled GEMM (the vanilla branch of the mining layer) against
+    an exact int32 product (cuBLAS int8, an implementation independent of
+    the kernel), rounded to bf16 once."""
+    g = torch.Generator().manual_seed(8 + m + n)
+    A = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int8).cuda()
+    B = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8).cuda()
+    sa, sb = (torch.rand(m, generator=g) / 64).cuda(), (torch.rand(n, generator=g) / 64).cuda()
     C = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
-    pg.gemm(A.cuda(), B.cuda(), sa.cuda(), sb.cuda(), C)
-    ref = (A.float() @ B.float().T) * sa[:, None] * sb[None, :]
-    torch.testing.assert_close(C.float().cpu(), ref.to(torch.bfloat16).float(), atol=ATOL, rtol=RTOL)
+    pg.gemm(A, B, sa, sb, C)
+    # _int_mm wants m > 16 and dims that are multiples of 8
+    mp = -(-m // 8) * 8
+    Ap = torch.zeros(mp, k, dtype=torch.int8, device="cuda")
+    Ap[:m] = A
+    np_ = -(-n // 8) * 8
+    Bp = torch.zeros(np_, k, dtype=torch.int8, device="cuda")
+    Bp[:n] = B
+    ab = torch._int_mm(Ap, Bp.t())[:m, :n].float()
+    ref = (ab * sa[:, None] * sb[None, :]).to(torch.bfloat16).float()
+    torch.testing.assert_close(C.float(), ref, atol=ATOL, rtol=RTOL)
 
 
 def test_torch_ops_schema_path():

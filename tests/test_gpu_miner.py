@@ -198,6 +198,40 @@ def test_pearl_linear_apply_weights_branches():
     torch.testing.assert_close(y8.float(), ref8.to(torch.bfloat16).float(), atol=ATOL, rtol=RTOL)
 
 
+def test_weight_root_cached_per_job_and_refreshed_after_a_write():
+    """A layer's weight is hashed once per job: a second GEMM of the same
+    weight reuses the root (same commitment seeds as a fresh hash, from the
+    oracle), and an in-place write to the weight makes the next GEMM hash
+    it again."""
+    class Layer:
+        pass
+
+    g = torch.Generator().manual_seed(18)
+    m, n, k = 384, 512, 1024
+    layer = Layer()
+    layer.weight = torch.randint(-63, 64, (n, k), generator=g, dtype=torch.int8).cuda()
+    layer.weight_scale = (torch.rand(n, 1, generator=g) / 64).cuda()
+    cfg = MN.MiningConfig(min_m=256, min_n=256, min_k=256)
+    key, _ = _job(16)
+    job = MN.MiningJob(key, 0, True)
+    lin = MN.PearlLinear(True, cfg, job)
+    for i in range(3):
+        if i == 2:
+            layer.weight.add_(1)  # a new version of the weight
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16).cuda()
+        lin.apply_weights(layer, x)
+        torch.cuda.synchronize()
+        xq, _, _ = MN.quant_7bit(x)
+        ra = O.tensor_hash(_np(xq), key)
+        rb = O.tensor_hash(_np(layer.weight), key)
+        seed_b, seed_a = O.commitment(key, ra, rb, salted_dims=(m, n))
+        assert _np(lin.mined[-1].commitment_hash_B).tobytes() == seed_b, i
+        assert _np(lin.mined[-1].commitment_hash_A).tobytes() == seed_a, i
+    assert len({id(v[1]) for v in MN._B_ROOTS.values()}) >= 2
+    for mnd in lin.mined:
+        MN.release_header(mnd.host_signal_header_pinned)
+
+
 # -------------------------------------------------------------- MoE GEMM1 ---
 def test_moe_gemm1_per_expert_parity():
     E, tokens, top_k, N, K, r = 4, 200, 2, 256, 512, 128
