@@ -373,6 +373,42 @@ PB2_API int pb2_noisy_gemm(const pb2_gemm_params* p, void* stream);
  * operands from p->ApEA / p->BpEB (the reference passes A and B there). */
 PB2_API int pb2_gemm(const pb2_gemm_params* p, void* stream);
 
+/* ---------------------------------------------------- grouped noisy_gemm ---
+ * Replaces the per-expert loop of the mined MoE GEMM1
+ * (miner/vllm-miner/src/vllm_miner/pearl_moe_experts.py:304-343, each pass a
+ * moe_gemm_operators.py:259-329 noisy_gemm with run_noising_A/B): the
+ * experts' mined GEMMs in one noising launch and one persistent main launch
+ * per 16 experts, with the same results as one pb2_noisy_gemm per expert.
+ * `shared` holds the stacked problem: m = all experts' rows, A-side arrays
+ * (A, EAL, ApEA, EAL_fp16, AxEBL_fp16, A_scales, C) with those m rows in
+ * expert order, B-side arrays (B, EBR, BpEB, EBR_fp16, EARxBpEB_fp16,
+ * B_scales) with n rows per expert (expert e at rows [e n, e n + n)), the
+ * shared K-side factors, r, k, pow_target, pow_key and the tile knobs; its
+ * host_signal_*, hits, transcripts and digests are not used.  Expert e
+ * takes rows [a_row0, a_row0 + m) of the A-side arrays (a_row0 = the sum of
+ * the earlier experts' m; m may be 0) and reports its hits through its own
+ * sync word, pinned header and optional hit list and debug dumps, indexed
+ * as for a pb2_noisy_gemm of its m rows.  A device timeout is recorded in
+ * the first non-empty expert's sync word.  Half-precision projections only
+ * (AxEBL_int32 / EARxBpEB_int32 NULL); skip_reduction, skip_denoising and
+ * enable_debug must be 0. */
+typedef struct pb2_expert_gemm {
+  int64_t m;
+  int64_t a_row0;
+  void* host_signal_header_pinned; /* optional */
+  void* host_signal_sync;          /* required when m > 0 */
+  uint32_t* hits;                  /* optional, hit_capacity * PB2_HIT_WORDS words */
+  int64_t hit_capacity;
+  uint32_t* transcripts;           /* optional, (m/2)*(n/64) * 16 words */
+  uint32_t* digests;               /* optional, (m/2)*(n/64) * 8 words */
+} pb2_expert_gemm;
+typedef struct pb2_grouped_gemm_params {
+  pb2_gemm_params shared;
+  int64_t num_experts;
+  const pb2_expert_gemm* experts; /* host array of num_experts entries */
+} pb2_grouped_gemm_params;
+PB2_API int pb2_noisy_gemm_grouped(const pb2_grouped_gemm_params* p, void* stream);
+
 /* ------------------------------------------- noisy_gemm, static scratch ---
  * No counterpart in the reference.  The same mined GEMM as pb2_noisy_gemm,
  * for callers that cannot allocate device memory: a host that only reaches

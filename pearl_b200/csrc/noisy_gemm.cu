@@ -57,27 +57,52 @@ constexpr int kCStageBytes = kFoldWarps * kCBoxBytes;
 constexpr int kTmemCols = 512;
 constexpr uint16_t kPairMask = 0x3;
 
+// What one launch shares: the B-side operands (the rows of every problem's
+// B), the shapes, the schedule and the hash inputs.
 struct MainArgs {
-  CUtensorMap tmA, tmB;      // ApEA (m,k), BpEB (n,k): int8, boxes of 128 rows
-  CUtensorMap tmDA0, tmDB0;  // EAL_fp16 (m,r), EARxBpEB_fp16 (n,r)
-  CUtensorMap tmDA1, tmDB1;  // AxEBL_fp16 (m,r), EBR_fp16 (n,r)
-  CUtensorMap tmC;           // C (m,n) bf16, 32 x 32 boxes, 64-byte swizzle
-  int M, N, K, R;
-  int tiles_m, tiles_n, num_tiles, group;
+  CUtensorMap tmB;           // BpEB (n_rows,k) int8
+  CUtensorMap tmDB0, tmDB1;  // EARxBpEB_fp16, EBR_fp16 (n_rows,r)
+  int N, K, R;               // N: columns of C (rows of B per problem)
+  int tiles_n, num_tiles, group;
   int tpr;  // tiles a CTA pair runs per round: 2 (two TMEM slots in alternation) or 1
-  const float* sA;
-  const float* sB;
-  __nv_bfloat16* C;
-  SignalSync* sync;
-  SignalHeader* header;
+  SignalSync* sync;  // where a timed-out wait records its error
   const uint32_t* target;
   const uint32_t* key;
   unsigned long long* counter;
+  long long wait_budget;  // SM cycles a device-side wait may spin (pb2_set_wait_budget_cycles)
+};
+
+// One GEMM of the launch: the whole problem of pb2_noisy_gemm, or one expert
+// of pb2_noisy_gemm_grouped (its rows of A and C, its n rows of B, its own
+// hit signalling).  The A-side tensor maps cover exactly the problem's rows,
+// so loads past its last row read the fill value and stores past it are
+// dropped, as in a launch of its own.
+struct ExpertEntry {
+  CUtensorMap tmA;           // ApEA rows (m,k) int8, boxes of 128 rows
+  CUtensorMap tmDA0, tmDA1;  // EAL_fp16, AxEBL_fp16 rows (m,r)
+  CUtensorMap tmC;           // C rows (m,N) bf16, 32 x 32 boxes, 64-byte swizzle
+  int m;                     // rows
+  int tiles_m;               // 256-row tiles
+  int tile_begin;            // its first tile in the launch's tile order
+  int b_row0;                // its first row of the B-side operands
+  const float* sA;           // its A_scales
+  const float* sB;           // its B_scales (N)
+  SignalSync* sync;
+  SignalHeader* header;
   uint32_t* hits;
   long long hit_cap;
   uint32_t* transcripts;
   uint32_t* digests;
-  long long wait_budget;  // SM cycles a device-side wait may spin (pb2_set_wait_budget_cycles)
+};
+constexpr int kMaxExperts = 16;  // experts of one grouped launch (kernel parameter space)
+template <int kE>
+struct ExpertTable {
+  int count;
+  ExpertEntry ex[kE];
+};
+
+struct TileRef {
+  int e, tm, tn;
 };
 
 struct Smem {
@@ -92,14 +117,24 @@ struct Smem {
   int abort_flag;
 };
 
-__device__ __forceinline__ void tile_coords(const MainArgs& a, int t, int& tm, int& tn) {
-  const int gsize = a.group * a.tiles_n;
-  const int g = t / gsize;
-  const int first_m = g * a.group;
-  const int gm = min(a.group, a.tiles_m - first_m);
-  const int within = t - g * gsize;
-  tm = first_m + within % gm;
-  tn = within / gm;
+// Tile t of the launch: its problem e and its (tm, tn) there.  Problems
+// follow one another in tile order; within one, a raster of `group` row
+// tiles walks all column tiles before the next group (L2 reuse of B).
+template <int kE>
+__device__ __forceinline__ TileRef tile_of(const MainArgs& a, const ExpertTable<kE>& x, int t) {
+  int e = 0;
+  if constexpr (kE > 1) {
+    while (e + 1 < x.count && t >= x.ex[e + 1].tile_begin) ++e;
+  }
+  const ExpertEntry& E = x.ex[e];
+  const int lt = t - E.tile_begin;
+  const int group = min(a.group, E.tiles_m);
+  const int gsize = group * a.tiles_n;
+  const int g = lt / gsize;
+  const int first_m = g * group;
+  const int gm = min(group, E.tiles_m - first_m);
+  const int within = lt - g * gsize;
+  return TileRef{e, first_m + within % gm, within / gm};
 }
 
 // Per-slot phase bits packed in one word (bit s = parity of slot s).
@@ -116,7 +151,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float x, float y) {
 // and columns >= N.  Writing C straight from registers would scatter every
 // store instruction over 32 rows, and the fold warps would spend thousands of
 // cycles in the store unit while the MMA issuer waits for their next release.
-__device__ __forceinline__ void store_c_packed(const MainArgs& a, uint8_t* box, const uint32_t* w,
+__device__ __forceinline__ void store_c_packed(const CUtensorMap* tmC, uint8_t* box, const uint32_t* w,
                                                int row0, int col0, int lane) {
   if (lane == 0) bulk_wait_read_all();  // the box's previous store has read it
   __syncwarp();
@@ -131,7 +166,7 @@ __device__ __forceinline__ void store_c_packed(const MainArgs& a, uint8_t* box, 
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0) {
-    tma_store_2d(&a.tmC, box, col0, row0);
+    tma_store_2d(tmC, box, col0, row0);
     bulk_commit_group();
   }
 }
@@ -139,13 +174,13 @@ __device__ __forceinline__ void store_c_packed(const MainArgs& a, uint8_t* box, 
 // Hit publication.  Rows are reported in the reference's 128-row tile
 // convention (tileCoord[0] = 128-row block, thread rows < 128), so
 // extract_indices() gives the same A rows as for the reference kernel.
-__device__ void publish_hit(const MainArgs& a, int tm128, int tn, int row_in_tile, int cls,
-                            const uint32_t* digest) {
+__device__ void publish_hit(const MainArgs& a, const ExpertEntry& E, int tm128, int tn, int row_in_tile,
+                            int cls, const uint32_t* digest) {
   const uint32_t row_off = uint32_t(tm128 * BMC + row_in_tile);
   const uint32_t col_off = uint32_t(tn * BN + 2 * cls);
-  const unsigned slot = atomicAdd(&a.sync->hit_count, 1u);
-  if (a.hits && (long long)slot < a.hit_cap) {
-    uint32_t* h = a.hits + size_t(slot) * PB2_HIT_WORDS;
+  const unsigned slot = atomicAdd(&E.sync->hit_count, 1u);
+  if (E.hits && (long long)slot < E.hit_cap) {
+    uint32_t* h = E.hits + size_t(slot) * PB2_HIT_WORDS;
     h[0] = row_off;
     h[1] = col_off;
     h[2] = uint32_t(tm128);
@@ -153,8 +188,8 @@ __device__ void publish_hit(const MainArgs& a, int tm128, int tn, int row_in_til
 #pragma unroll
     for (int i = 0; i < 8; ++i) h[4 + i] = digest[i];
   }
-  if (a.header && atomicCAS(&a.sync->global_lock, 0, 1) == 0) {
-    SignalHeader* H = a.header;
+  if (E.header && atomicCAS(&E.sync->global_lock, 0, 1) == 0) {
+    SignalHeader* H = E.header;
     H->gridDim[0] = gridDim.x; H->gridDim[1] = gridDim.y; H->gridDim[2] = gridDim.z;
     H->blockDim[0] = blockDim.x; H->blockDim[1] = blockDim.y; H->blockDim[2] = blockDim.z;
     H->blockIdx[0] = blockIdx.x; H->blockIdx[1] = blockIdx.y; H->blockIdx[2] = blockIdx.z;
@@ -167,13 +202,13 @@ __device__ void publish_hit(const MainArgs& a, int tm128, int tn, int row_in_til
       H->thread_rows[j] = uint8_t(row_in_tile + 8 * ((j >> 1) & 1));
       H->thread_cols[j] = uint8_t(2 * cls + (j & 1) + 8 * (j >> 2));
     }
-    H->mma_size[0] = a.M; H->mma_size[1] = a.N; H->mma_size[2] = a.K;
+    H->mma_size[0] = E.m; H->mma_size[1] = a.N; H->mma_size[2] = a.K;
     H->mma_tile_size[0] = BMC; H->mma_tile_size[1] = BN; H->mma_tile_size[2] = kTileK;
     for (int i = 0; i < 8; ++i) H->target[i] = a.target[i];
     __threadfence_system();
     H->status = 1;
     __threadfence_system();
-    atomicExch(&a.sync->status, 1);
+    atomicExch(&E.sync->status, 1);
   }
 }
 
@@ -186,8 +221,12 @@ __device__ void publish_hit(const MainArgs& a, int tm128, int tn, int row_in_til
 // than two 256-wide tiles per SM pair: a decode batch), where narrower tiles
 // put more of the 148 SMs to work; the transcript and denoise variants
 // always use 256 (the hash-tile column period).
-template <int BK, int kSPU, bool kReduce, bool kDenoise, bool kDebug, int kTN>
-__global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_constant__ MainArgs a) {
+//
+// kE = problems per launch: 1, or up to kMaxExperts (the grouped MoE GEMM:
+// every expert's tiles in one persistent launch, x.ex[e] per expert).
+template <int BK, int kSPU, bool kReduce, bool kDenoise, bool kDebug, int kTN, int kE>
+__global__ void __launch_bounds__(kThreads, 1)
+    noisy_gemm_kernel(const __grid_constant__ MainArgs a, const __grid_constant__ ExpertTable<kE> x) {
   static_assert(kTN == BN || (kTN == BN / 2 && !kReduce && !kDenoise), "narrow tiles: plain GEMM only");
   constexpr int kAStage = BMC * BK;        // this CTA's 128 rows of A
   constexpr int kBStage = (kTN / 2) * BK;  // this CTA's half of the tile's rows of B
@@ -238,12 +277,18 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch(&a.tmA);
     tma_prefetch(&a.tmB);
-    tma_prefetch(&a.tmC);
     if (kDenoise) {
-      tma_prefetch(&a.tmDA0); tma_prefetch(&a.tmDB0);
-      tma_prefetch(&a.tmDA1); tma_prefetch(&a.tmDB1);
+      tma_prefetch(&a.tmDB0);
+      tma_prefetch(&a.tmDB1);
+    }
+    if constexpr (kE == 1) {
+      tma_prefetch(&x.ex[0].tmA);
+      tma_prefetch(&x.ex[0].tmC);
+      if (kDenoise) {
+        tma_prefetch(&x.ex[0].tmDA0);
+        tma_prefetch(&x.ex[0].tmDA1);
+      }
     }
   }
   if (warp == 1) {
@@ -282,18 +327,20 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
       bool ok = true;
       for (int t0 = first; t0 < a.num_tiles && ok; t0 += stride) {
         const bool two = a.tpr == 2 && t0 + 1 < a.num_tiles;
-        int tm0, tn0, tm1 = 0, tn1 = 0;
-        tile_coords(a, t0, tm0, tn0);
-        if (two) tile_coords(a, t0 + 1, tm1, tn1);
-        // This CTA's 128 rows of A and half of the B rows, per slot.
-        const int ma = tm0 * BM + int(rank) * BMC, na = tn0 * kTN + int(rank) * (kTN / 2);
-        const int mb = tm1 * BM + int(rank) * BMC, nb = tn1 * kTN + int(rank) * (kTN / 2);
+        const TileRef r0 = tile_of(a, x, t0);
+        const TileRef r1 = two ? tile_of(a, x, t0 + 1) : r0;
+        const ExpertEntry& Ea = x.ex[r0.e];
+        const ExpertEntry& Eb = x.ex[r1.e];
+        // This CTA's 128 rows of A (of its problem) and half of the B rows, per slot.
+        const int ma = r0.tm * BM + int(rank) * BMC, na = Ea.b_row0 + r0.tn * kTN + int(rank) * (kTN / 2);
+        const int mb = r1.tm * BM + int(rank) * BMC, nb = Eb.b_row0 + r1.tn * kTN + int(rank) * (kTN / 2);
         // Main units, then the denoise units, in the issuer's order.  The two
         // loops are kept apart (and the tensor maps named, not selected), so
         // the per-stage code on the main path stays minimal.
         for (int u = 0; u < nmain && ok; ++u) {
           for (int s = 0; s < (two ? 2 : 1) && ok; ++s) {
             const int m0 = s ? mb : ma, n0 = s ? nb : na;
+            const CUtensorMap* tmA = s ? &Eb.tmA : &Ea.tmA;
             for (int st = 0; st < stages_per_unit; ++st, ++it) {
               const int j = it % kStages;
               if (!(ok = mbar_wait_warp(&S.empty[j], ((it / kStages) & 1) ^ 1, abort_flag, a.sync, a.wait_budget))) break;
@@ -302,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
               if (leader) {
                 // The leader CTA's full barrier counts both CTAs' bytes.
                 if (rank == 0) mbar_arrive_expect_tx(&S.full[j], 2 * kStageBytes);
-                tma_load_2d_2sm(&a.tmA, &S.full[j], sa, kbyte, m0);
+                tma_load_2d_2sm(tmA, &S.full[j], sa, kbyte, m0);
                 tma_load_2d_2sm(&a.tmB, &S.full[j], sa + kAStage, kbyte, n0);
               }
             }
@@ -312,6 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
           for (int d = 0; d < nden && ok; ++d) {
             for (int s = 0; s < (two ? 2 : 1) && ok; ++s) {
               const int m0 = s ? mb : ma, n0 = s ? nb : na;
+              const ExpertEntry& Es = s ? Eb : Ea;
               for (int st = 0; st < stages_per_unit; ++st, ++it) {
                 const int j = it % kStages;
                 if (!(ok = mbar_wait_warp(&S.empty[j], ((it / kStages) & 1) ^ 1, abort_flag, a.sync, a.wait_budget))) break;
@@ -321,10 +369,10 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
                 if (leader) {
                   if (rank == 0) mbar_arrive_expect_tx(&S.full[j], 2 * kStageBytes);
                   if (ds < den_stages_per_product) {
-                    tma_load_2d_2sm(&a.tmDA0, &S.full[j], sa, col, m0);
+                    tma_load_2d_2sm(&Es.tmDA0, &S.full[j], sa, col, m0);
                     tma_load_2d_2sm(&a.tmDB0, &S.full[j], sa + kAStage, col, n0);
                   } else {
-                    tma_load_2d_2sm(&a.tmDA1, &S.full[j], sa, col, m0);
+                    tma_load_2d_2sm(&Es.tmDA1, &S.full[j], sa, col, m0);
                     tma_load_2d_2sm(&a.tmDB1, &S.full[j], sa + kAStage, col, n0);
                   }
                 }
@@ -462,7 +510,9 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
     // so comes within kStages units of refilling the stage, only after these
     // warps release it.  Lone events (the f32 rewrite without a transcript,
     // the final store) have no such neighbour and wait on acc_full instead.
-    auto fold_slot = [&](auto slot, int round, int u, int tm, int tn, uint32_t last_stage) {
+    auto fold_slot = [&](auto slot, int round, int u, const TileRef& tr, uint32_t last_stage) {
+      const int tm = tr.tm, tn = tr.tn;
+      const ExpertEntry& E = x.ex[tr.e];
       constexpr int s = decltype(slot)::value;
       const int b = 2 * s + (round & 1);  // transcript buffer
       const bool is_main = u < nmain;
@@ -521,7 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
         atomicXor(tw + 16, __funnelshift_l(f1, f1, rot));
         // The reference counts one hash per 2 x 64 tile of each 128-row
         // tile that starts inside M.
-        if (kDebug && lane == 0 && tm * BM + int(rank) * BMC < a.M) atomicAdd(a.counter, 16ull);
+        if (kDebug && lane == 0 && tm * BM + int(rank) * BMC < E.m) atomicAdd(a.counter, 16ull);
         if (last_main) {
           __syncwarp();
           if (lane == 0) mbar_arrive(&S.xready[b]);  // this warp's contributions are in
@@ -562,9 +612,9 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
       float2 sbv = make_float2(0.f, 0.f);
       if (do_store) {  // scales first: their latency overlaps the loads
         const int row = tm * BM + int(rank) * BMC + 32 * q + lane;
-        rs = (row < a.M ? a.sA[row] : 0.0f) * (is_main ? 1.0f : 4096.0f);
+        rs = (row < E.m ? E.sA[row] : 0.0f) * (is_main ? 1.0f : 4096.0f);
         const int c = tn * kTN + 64 * wi + 2 * lane;  // this lane's two column scales
-        if (c < a.N) sbv = *reinterpret_cast<const float2*>(a.sB + c);
+        if (c < a.N) sbv = *reinterpret_cast<const float2*>(E.sB + c);
       }
       const int row0 = tm * BM + int(rank) * BMC + 32 * q;
       uint8_t* box = cstage + fw * kCBoxBytes;
@@ -596,7 +646,7 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
             const float f1 = is_main ? float(int(v[i + 1])) : __uint_as_float(v[i + 1]);
             packed[i / 2] = pack_bf16(f0 * rs * bx, f1 * rs * by);
           }
-          store_c_packed(a, box, packed, row0, tn * kTN + 64 * wi + 32 * h, lane);
+          store_c_packed(&E.tmC, box, packed, row0, tn * kTN + 64 * wi + 32 * h, lane);
         }
       }
       if (do_convert) tmem_wait_st();
@@ -607,9 +657,8 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
     uint32_t it = 0;  // operand stages issued so far, in the issuer's order
     for (int t0 = first; t0 < a.num_tiles && ok; t0 += stride) {
       const bool two = a.tpr == 2 && t0 + 1 < a.num_tiles;
-      int tm0, tn0, tm1 = 0, tn1 = 0;
-      tile_coords(a, t0, tm0, tn0);
-      if (two) tile_coords(a, t0 + 1, tm1, tn1);
+      const TileRef r0 = tile_of(a, x, t0);
+      const TileRef r1 = two ? tile_of(a, x, t0 + 1) : r0;
       const int round = (t0 - first) / stride;
       for (int u = 0; u < units && ok; ++u) {
         const bool is_main = u < nmain;
@@ -617,8 +666,8 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
         const uint32_t it0 = it;
         it += uint32_t((two ? 2 : 1) * stages_per_unit);
         if (!event) continue;
-        fold_slot(I0{}, round, u, tm0, tn0, it0 + stages_per_unit - 1);
-        if (two && ok) fold_slot(I1{}, round, u, tm1, tn1, it0 + 2 * stages_per_unit - 1);
+        fold_slot(I0{}, round, u, r0, it0 + stages_per_unit - 1);
+        if (two && ok) fold_slot(I1{}, round, u, r1, it0 + 2 * stages_per_unit - 1);
       }
     }
     if (lane == 0) bulk_wait_all();  // C is written before the kernel ends
@@ -630,7 +679,9 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
     // it is read, for the slot's tile two rounds later.
     const int j = (warp - 2 - kFoldWarps) * 32 + lane;
     bool ok = true;
-    auto hash_buffer = [&](auto slot, int round, int tm, int tn) {
+    auto hash_buffer = [&](auto slot, int round, const TileRef& tr) {
+      const int tm = tr.tm, tn = tr.tn;
+      const ExpertEntry& E = x.ex[tr.e];
       const int b = 2 * decltype(slot)::value + (round & 1);
       if (!(ok = mbar_wait_idle_warp(&S.xready[b], (round >> 1) & 1, abort_flag, a.sync, a.wait_budget))) return;
       const int tm128 = 2 * tm + int(rank);
@@ -651,15 +702,15 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
         const int row_in_tile = 32 * hq + (p & 7) + 16 * (p >> 3);
         const int64_t grow = int64_t(tm128) * BMC + row_in_tile;
         const int64_t gcol = int64_t(tn) * BN + 2 * cls;
-        const bool in_bounds = (grow + 8 < a.M) && (gcol + 249 < a.N);
-        if (in_bounds && (a.transcripts || a.digests)) {
+        const bool in_bounds = (grow + 8 < E.m) && (gcol + 249 < a.N);
+        if (in_bounds && (E.transcripts || E.digests)) {
           const int64_t idx = (grow / 16 * 8 + grow % 16) * (a.N / 64) + gcol / 256 * 4 + (gcol % 256) / 2;
-          if (a.transcripts)
-            for (int k = 0; k < 16; ++k) a.transcripts[idx * 16 + k] = T[k];
-          if (a.digests)
-            for (int k = 0; k < 8; ++k) a.digests[idx * 8 + k] = dg[k];
+          if (E.transcripts)
+            for (int k = 0; k < 16; ++k) E.transcripts[idx * 16 + k] = T[k];
+          if (E.digests)
+            for (int k = 0; k < 8; ++k) E.digests[idx * 8 + k] = dg[k];
         }
-        if (in_bounds && u256_le(dg, a.target)) publish_hit(a, tm128, tn, row_in_tile, cls, dg);
+        if (in_bounds && u256_le(dg, a.target)) publish_hit(a, E, tm128, tn, row_in_tile, cls, dg);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.xfree[b]);
@@ -667,11 +718,10 @@ __global__ void __launch_bounds__(kThreads, 1) noisy_gemm_kernel(const __grid_co
     for (int t0 = first; t0 < a.num_tiles && ok; t0 += stride) {
       const bool two = a.tpr == 2 && t0 + 1 < a.num_tiles;
       const int round = (t0 - first) / stride;
-      int tm0, tn0, tm1 = 0, tn1 = 0;
-      tile_coords(a, t0, tm0, tn0);
-      if (two) tile_coords(a, t0 + 1, tm1, tn1);
-      hash_buffer(I0{}, round, tm0, tn0);
-      if (two && ok) hash_buffer(I1{}, round, tm1, tn1);
+      const TileRef r0 = tile_of(a, x, t0);
+      const TileRef r1 = two ? tile_of(a, x, t0 + 1) : r0;
+      hash_buffer(I0{}, round, r0);
+      if (two && ok) hash_buffer(I1{}, round, r1);
     }
   }
 
@@ -694,9 +744,9 @@ int& resident_pairs(int device) {
   return cached[device & 63];
 }
 
-template <int BK, int SPU, bool R_, bool D_, bool G_, int TN = BN>
-int launch_variant(const MainArgs& a, int device, cudaStream_t s) {
-  auto kern = noisy_gemm_kernel<BK, SPU, R_, D_, G_, TN>;
+template <int BK, int SPU, bool R_, bool D_, bool G_, int TN, int kE>
+int launch_variant(const MainArgs& a, const ExpertTable<kE>& x, int device, cudaStream_t s) {
+  auto kern = noisy_gemm_kernel<BK, SPU, R_, D_, G_, TN, kE>;
   const int smem = stage_budget(R_) + (R_ ? kXbufBytes : 0) + kCStageBytes + int(sizeof(Smem)) + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return launch_status();
@@ -712,7 +762,7 @@ int launch_variant(const MainArgs& a, int device, cudaStream_t s) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   // A persistent grid: as many CTA pairs as can be co-resident (SM pairs in
-  // one GPC), never more than half the tiles (each pair runs two slots).
+  // one GPC), never more than the tiles need (a pair runs tpr per round).
   int resident = resident_pairs(device);
   if (resident == 0) {
     cfg.gridDim = dim3(2, 1, 1);
@@ -732,23 +782,74 @@ int launch_variant(const MainArgs& a, int device, cudaStream_t s) {
   attrs[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = 2;
-  cudaLaunchKernelEx(&cfg, kern, a);
+  cudaLaunchKernelEx(&cfg, kern, a, x);
   return launch_status();
 }
 
 template <int BK, int SPU>
-int launch_spu(const MainArgs& a, int device, bool reduce, bool denoise, bool debug, bool narrow,
-               cudaStream_t s) {
-  if (narrow) return launch_variant<BK, SPU, false, false, false, BN / 2>(a, device, s);
-  if (reduce && denoise) return debug ? launch_variant<BK, SPU, true, true, true>(a, device, s)
-                                      : launch_variant<BK, SPU, true, true, false>(a, device, s);
-  if (reduce) return debug ? launch_variant<BK, SPU, true, false, true>(a, device, s)
-                           : launch_variant<BK, SPU, true, false, false>(a, device, s);
-  if (denoise) return launch_variant<BK, SPU, false, true, false>(a, device, s);
-  return launch_variant<BK, SPU, false, false, false>(a, device, s);
+int launch_spu(const MainArgs& a, const ExpertTable<1>& x, int device, bool reduce, bool denoise, bool debug,
+               bool narrow, cudaStream_t s) {
+  if (narrow) return launch_variant<BK, SPU, false, false, false, BN / 2, 1>(a, x, device, s);
+  if (reduce && denoise) return debug ? launch_variant<BK, SPU, true, true, true, BN, 1>(a, x, device, s)
+                                      : launch_variant<BK, SPU, true, true, false, BN, 1>(a, x, device, s);
+  if (reduce) return debug ? launch_variant<BK, SPU, true, false, true, BN, 1>(a, x, device, s)
+                           : launch_variant<BK, SPU, true, false, false, BN, 1>(a, x, device, s);
+  if (denoise) return launch_variant<BK, SPU, false, true, false, BN, 1>(a, x, device, s);
+  return launch_variant<BK, SPU, false, false, false, BN, 1>(a, x, device, s);
+}
+
+// The A-side tensor maps and scalars of one problem: rows [0, m) of the
+// A-side arrays starting at the given pointers.
+int make_entry(ExpertEntry& e, const void* ApEA, const void* EAL_fp16, const void* AxEBL_fp16, const float* sA,
+               void* C, int64_t m, int64_t n, int64_t k, int64_t r, int bk, bool denoise) {
+  const CUtensorMapSwizzle swz = bk == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  int st;
+  if ((st = make_tmap_2d(&e.tmA, ApEA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, k, m, bk, BMC, swz))) return st;
+  if ((st = make_tmap_2d(&e.tmC, C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, n, m, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)))
+    return st;
+  if (denoise) {
+    const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const int dc = bk / 2;  // fp16 elements per stage row
+    if ((st = make_tmap_2d(&e.tmDA0, EAL_fp16, F16, 2, r, m, dc, BMC, swz)) ||
+        (st = make_tmap_2d(&e.tmDA1, AxEBL_fp16, F16, 2, r, m, dc, BMC, swz)))
+      return st;
+  }
+  e.m = int(m);
+  e.tiles_m = int((m + BM - 1) / BM);
+  e.sA = sA;
+  return PB2_OK;
 }
 
 bool al16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+// The launch-wide arguments: B-side tensor maps (n rows per problem; the
+// grouped launch passes all problems' rows in one array), shapes and the
+// hash inputs.
+int make_shared_args(MainArgs& a, const pb2_gemm_params& p, int bk, int tn_width, bool denoise,
+                     int64_t b_rows = -1) {
+  if (b_rows < 0) b_rows = p.n;
+  const CUtensorMapSwizzle swz = bk == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  int st;
+  if ((st = make_tmap_2d(&a.tmB, p.BpEB, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.k, b_rows, bk, tn_width / 2, swz)))
+    return st;
+  if (denoise) {
+    const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const int dc = bk / 2;
+    if ((st = make_tmap_2d(&a.tmDB0, p.EARxBpEB_fp16, F16, 2, p.r, b_rows, dc, BN / 2, swz)) ||
+        (st = make_tmap_2d(&a.tmDB1, p.EBR_fp16, F16, 2, p.r, b_rows, dc, BN / 2, swz)))
+      return st;
+  }
+  a.N = int(p.n);
+  a.K = int(p.k);
+  a.R = int(p.r);
+  a.tiles_n = int((p.n + tn_width - 1) / tn_width);
+  a.group = p.swizzle > 0 ? p.swizzle : 8;
+  a.target = p.pow_target;
+  a.key = p.pow_key;
+  a.counter = reinterpret_cast<unsigned long long*>(p.inner_hash_counter);
+  a.wait_budget = wait_budget_cycles();
+  return PB2_OK;
+}
 
 }  // namespace
 
@@ -795,60 +896,98 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
   const int pairs_est = resident_pairs(p.device) ? resident_pairs(p.device) : std::max(1, sm_count(p.device) / 2);
   const bool narrow = !reduce && !denoise && tiles_m * ((p.n + BN - 1) / BN) < 2 * int64_t(pairs_est);
   const int tn_width = narrow ? BN / 2 : BN;
-  const CUtensorMapSwizzle swz = bk == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   MainArgs a;
   std::memset(&a, 0, sizeof(a));
+  ExpertTable<1> x;
+  std::memset(&x, 0, sizeof(x));
   int st;
-  if ((st = make_tmap_2d(&a.tmA, p.ApEA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.k, p.m, bk, BMC, swz)))
+  if ((st = make_shared_args(a, p, bk, tn_width, denoise))) return st;
+  if ((st = make_entry(x.ex[0], p.ApEA, p.EAL_fp16, p.AxEBL_fp16, p.A_scales, p.C, p.m, p.n, p.k, p.r, bk,
+                       denoise)))
     return st;
-  if ((st = make_tmap_2d(&a.tmB, p.BpEB, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.k, p.n, bk, tn_width / 2, swz)))
-    return st;
-  if ((st = make_tmap_2d(&a.tmC, p.C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.n, p.m, 32, 32,
-                         CU_TENSOR_MAP_SWIZZLE_64B)))
-    return st;
-  if (denoise) {
-    const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    const int dc = bk / 2;  // fp16 elements per stage row
-    if ((st = make_tmap_2d(&a.tmDA0, p.EAL_fp16, F16, 2, p.r, p.m, dc, BMC, swz)) ||
-        (st = make_tmap_2d(&a.tmDB0, p.EARxBpEB_fp16, F16, 2, p.r, p.n, dc, BN / 2, swz)) ||
-        (st = make_tmap_2d(&a.tmDA1, p.AxEBL_fp16, F16, 2, p.r, p.m, dc, BMC, swz)) ||
-        (st = make_tmap_2d(&a.tmDB1, p.EBR_fp16, F16, 2, p.r, p.n, dc, BN / 2, swz)))
-      return st;
-  }
-  a.M = int(p.m);
-  a.N = int(p.n);
-  a.K = int(p.k);
-  a.R = int(p.r);
-  a.tiles_m = int((p.m + BM - 1) / BM);
-  a.tiles_n = int((p.n + tn_width - 1) / tn_width);
-  a.num_tiles = a.tiles_m * a.tiles_n;
+  x.count = 1;
+  ExpertEntry& e = x.ex[0];
+  e.tile_begin = 0;
+  e.b_row0 = 0;
+  e.sB = p.B_scales;
+  e.sync = static_cast<SignalSync*>(p.host_signal_sync);
+  e.header = static_cast<SignalHeader*>(p.host_signal_header_pinned);
+  e.hits = p.hits;
+  e.hit_cap = p.hits ? p.hit_capacity : 0;
+  e.transcripts = p.transcripts;
+  e.digests = p.digests;
+  a.num_tiles = e.tiles_m * a.tiles_n;
   a.tpr = (narrow && a.num_tiles <= pairs_est) ? 1 : 2;
-  a.group = p.swizzle > 0 ? p.swizzle : 8;
-  if (a.group > a.tiles_m) a.group = a.tiles_m;
-  a.sA = p.A_scales;
-  a.sB = p.B_scales;
-  a.C = static_cast<__nv_bfloat16*>(p.C);
-  a.sync = static_cast<SignalSync*>(p.host_signal_sync);
-  a.header = static_cast<SignalHeader*>(p.host_signal_header_pinned);
-  a.target = p.pow_target;
-  a.key = p.pow_key;
-  a.counter = reinterpret_cast<unsigned long long*>(p.inner_hash_counter);
-  a.hits = p.hits;
-  a.hit_cap = p.hits ? p.hit_capacity : 0;
-  a.transcripts = p.transcripts;
-  a.digests = p.digests;
-  a.wait_budget = wait_budget_cycles();
+  a.sync = e.sync;
 
   // Operand stages per unit: a unit is R bytes of K with transcript or
   // denoise (R = 64: one 64-byte stage; R = 128: one; R = 256: two), else
   // one 128-byte tile_size_k.
   const int spu = (reduce || denoise) ? int(p.r) / bk : kTileK / bk;
-  if (bk == 64) return launch_spu<64, 1>(a, p.device, reduce, denoise, debug, false, s);
-  return spu == 2 ? launch_spu<128, 2>(a, p.device, reduce, denoise, debug, false, s)
-                  : launch_spu<128, 1>(a, p.device, reduce, denoise, debug, narrow, s);
+  if (bk == 64) return launch_spu<64, 1>(a, x, p.device, reduce, denoise, debug, false, s);
+  return spu == 2 ? launch_spu<128, 2>(a, x, p.device, reduce, denoise, debug, false, s)
+                  : launch_spu<128, 1>(a, x, p.device, reduce, denoise, debug, narrow, s);
+}
+
+// The mined GEMMs of several problems that share B's K-side noise and the
+// hash inputs -- the experts of a MoE layer -- in persistent launches of up
+// to kMaxExperts problems each.  Problem e reads rows [a_row0_e, a_row0_e +
+// m_e) of the A-side arrays (ApEA, EAL_fp16, AxEBL_fp16, A_scales, C) and rows
+// [e n, e n + n) of the B-side ones (BpEB, EARxBpEB_fp16, EBR_fp16,
+// B_scales), and signals its hits through its own buffers.
+int run_grouped_kernel(const pb2_gemm_params& p, const pb2_expert_gemm* experts, int64_t num_experts,
+                       cudaStream_t s) {
+  const int bk = p.r == 64 ? 64 : 128;
+  const int spu = int(p.r) / bk;
+  for (int64_t e0 = 0; e0 < num_experts; e0 += kMaxExperts) {
+    const int cnt = int(std::min<int64_t>(kMaxExperts, num_experts - e0));
+    MainArgs a;
+    std::memset(&a, 0, sizeof(a));
+    ExpertTable<kMaxExperts> x;
+    std::memset(&x, 0, sizeof(x));
+    int st;
+    if ((st = make_shared_args(a, p, bk, BN, true, num_experts * p.n))) return st;
+    int tiles = 0;
+    SignalSync* first_sync = nullptr;
+    for (int i = 0; i < cnt; ++i) {
+      const pb2_expert_gemm& q = experts[e0 + i];
+      ExpertEntry& e = x.ex[i];
+      e.tile_begin = tiles;
+      e.b_row0 = int((e0 + i) * p.n);
+      e.sB = p.B_scales + (e0 + i) * p.n;
+      if (q.m > 0) {
+        const int64_t r0 = q.a_row0;
+        if ((st = make_entry(e, p.ApEA + r0 * p.k, static_cast<const uint16_t*>(p.EAL_fp16) + r0 * p.r,
+                             static_cast<uint16_t*>(p.AxEBL_fp16) + r0 * p.r, p.A_scales + r0,
+                             static_cast<uint16_t*>(p.C) + r0 * p.n, q.m, p.n, p.k, p.r, bk, true)))
+          return st;
+      }
+      e.sync = static_cast<SignalSync*>(q.host_signal_sync);
+      e.header = static_cast<SignalHeader*>(q.host_signal_header_pinned);
+      e.hits = q.hits;
+      e.hit_cap = q.hits ? q.hit_capacity : 0;
+      e.transcripts = q.transcripts;
+      e.digests = q.digests;
+      if (!first_sync && q.m > 0) first_sync = e.sync;
+      tiles += e.tiles_m * a.tiles_n;
+    }
+    if (tiles == 0) continue;
+    x.count = cnt;
+    a.num_tiles = tiles;
+    a.tpr = 2;
+    a.sync = first_sync;
+    int dev = p.device;
+    if (bk == 64) st = launch_variant<64, 1, true, true, false, BN, kMaxExperts>(a, x, dev, s);
+    else if (spu == 2) st = launch_variant<128, 2, true, true, false, BN, kMaxExperts>(a, x, dev, s);
+    else st = launch_variant<128, 1, true, true, false, BN, kMaxExperts>(a, x, dev, s);
+    if (st) return st;
+  }
+  return PB2_OK;
 }
 
 int denoise_convert(const int32_t* in, void* out, int64_t count, float scale, cudaStream_t s);
+int run_grouped_kernel(const pb2_gemm_params& p, const pb2_expert_gemm* experts, int64_t num_experts,
+                       cudaStream_t s);
 int run_noising_both(const pb2_noising_params& pa, const pb2_noising_params& pb, cudaStream_t stream);
 
 }  // namespace pb2
@@ -905,4 +1044,56 @@ extern "C" int pb2_gemm(const pb2_gemm_params* pp, void* stream) {
   int st = set_device(pp->device);
   if (st) return st;
   return run_main_kernel(*pp, false, false, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int pb2_noisy_gemm_grouped(const pb2_grouped_gemm_params* gp, void* stream) {
+  using namespace pb2;
+  if (!gp || !gp->experts || gp->num_experts <= 0) return PB2_ERR_INVALID_ARGUMENT;
+  const pb2_gemm_params& p = gp->shared;
+  const int64_t E = gp->num_experts;
+  if (p.skip_reduction || p.skip_denoising || p.enable_debug) return PB2_ERR_UNSUPPORTED_CONFIG;
+  if (p.AxEBL_int32 || p.EARxBpEB_int32) return PB2_ERR_UNSUPPORTED_CONFIG;  // half projections only
+  // The expert row ranges tile [0, p.m) in order, without gaps or overlap.
+  int64_t next = 0;
+  for (int64_t i = 0; i < E; ++i) {
+    const pb2_expert_gemm& q = gp->experts[i];
+    if (q.m < 0 || q.a_row0 != next) return PB2_ERR_INVALID_ARGUMENT;
+    if (q.m > 0 && (!q.host_signal_sync || (q.a_row0 * p.k) % 16 || (q.a_row0 * p.n * 2) % 16 ||
+                    (q.a_row0 * p.r * 2) % 16))
+      return PB2_ERR_INVALID_ARGUMENT;
+    if ((q.transcripts || q.digests) && (q.m % 16 != 0 || p.n % 256 != 0)) return PB2_ERR_INVALID_ARGUMENT;
+    next += q.m;
+  }
+  if (next != p.m) return PB2_ERR_INVALID_ARGUMENT;
+  // The shared checks on the stacked problem (all rows of A, n rows of B
+  // per expert): a rejected call queues no work.
+  pb2_gemm_params all = p;
+  all.host_signal_sync = gp->experts[0].host_signal_sync ? gp->experts[0].host_signal_sync : &all;
+  all.hits = nullptr;
+  all.transcripts = nullptr;
+  all.digests = nullptr;
+  int st = check_noisy_gemm_args(all);
+  if (st) return st;
+  if (E * p.n > INT32_MAX) return PB2_ERR_INVALID_ARGUMENT;
+  if ((st = set_device(p.device))) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Noising: row-independent, so one noise_A over every expert's rows and
+  // one noise_B over every expert's rows of B give each expert's operands.
+  pb2_noising_params qa{}, qb{};
+  qa.device = p.device; qa.rows = p.m; qa.k = p.k; qa.r = p.r;
+  qa.X = p.A; qa.EL = p.EAL; qa.E_rmajor = p.EAR_R_major; qa.E_kmajor = p.EBL_K_major;
+  qa.XpE = p.ApEA; qa.proj = p.AxEBL_fp16; qa.proj_is_fp16 = 1;
+  qa.host_signal_sync = all.host_signal_sync == &all ? nullptr : all.host_signal_sync;
+  qb.device = p.device; qb.rows = E * p.n; qb.k = p.k; qb.r = p.r;
+  qb.X = p.B; qb.EL = p.EBR; qb.E_rmajor = p.EBL_R_major; qb.E_kmajor = p.EAR_K_major;
+  qb.XpE = p.BpEB; qb.proj = p.EARxBpEB_fp16; qb.proj_is_fp16 = 1;
+  qb.host_signal_sync = qa.host_signal_sync;
+  if (p.run_noising_a && p.run_noising_b) {
+    if ((st = run_noising_both(qa, qb, s))) return st;
+  } else if (p.run_noising_a) {
+    if ((st = pb2_noise_A(&qa, stream))) return st;
+  } else if (p.run_noising_b) {
+    if ((st = pb2_noise_B(&qb, stream))) return st;
+  }
+  return run_grouped_kernel(p, gp->experts, E, s);
 }

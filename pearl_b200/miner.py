@@ -30,6 +30,7 @@ import torch
 from . import pearl_gemm_interface as P
 from .helpers import HostSignalHeaderPinnedPool, get_host_signal_sync_fields
 from .moe import build_routing_data, get_build_routing_data_scratchpad_bytes, scatter_rows
+from .moe import noisy_gemm_grouped as grouped_noisy_gemm
 from .quantization import quantize
 
 MAX_VAL_7BIT = 63
@@ -434,11 +435,14 @@ class MoEGemm1Result:
 
 
 def moe_gemm1(A_q, A_scales, topk_ids, w1, w1_scale, job: MiningJob,
-              config: MiningConfig = MiningConfig(), *, out=None, hit_capacity: int = 0):
+              config: MiningConfig = MiningConfig(), *, out=None, hit_capacity: int = 0,
+              grouped: bool = True):
     """Mined MoE GEMM1 (pearl_moe_experts.py:262-375): w1 (E, N, K) int7,
     w1_scale (E, N) or (E, N, 1) fp32, topk_ids (M, top_k).  Returns the
     per-slot output (M * top_k, N) bf16 in flat slot order and the per-expert
-    mining products.  Experts run one mined GEMM each, as in the reference."""
+    mining products.  ``grouped`` runs every expert's mined GEMM in one
+    grouped launch (pb2_noisy_gemm_grouped); without it, one mined GEMM per
+    expert as in the reference's loop.  Both give the same results."""
     E, N, K = w1.shape
     num_tokens = A_q.shape[0]
     top_k = topk_ids.shape[1]
@@ -451,6 +455,34 @@ def moe_gemm1(A_q, A_scales, topk_ids, w1, w1_scale, job: MiningJob,
         out = torch.empty((num_tokens * top_k, N), dtype=torch.bfloat16, device=A_q.device)
     by_slot = torch.empty_like(out)
     res = MoEGemm1Result(ctx)
+    if grouped:
+        # Every expert's mined GEMM in one noising and one persistent launch
+        # (pb2_noisy_gemm_grouped); the same results as the loop below.
+        dev = A_q.device
+        r = ctx.noise_rank
+        counts = [layout.expert_slice(e)[1] for e in range(E)]
+        m_all = A_e_all.shape[0]
+        syncs = torch.zeros(E, P.get_host_signal_sync_size(), dtype=torch.int8, device=dev)
+        headers = [_pinned_header() if counts[e] else None for e in range(E)]
+        hits = ([torch.zeros(hit_capacity, 12, dtype=torch.uint32, device=dev) if counts[e] else None
+                 for e in range(E)] if hit_capacity else None)
+        grouped_noisy_gemm(
+            A_e_all, B_stacked, EAL_e_all, EAL16_e_all, ctx.EBR, ctx.EBR_fp16, ctx.EAR_R_major,
+            ctx.EBL_R_major, ctx.EAR_K_major, ctx.EBL_K_major,
+            torch.empty((m_all, r), dtype=torch.float16, device=dev),
+            torch.empty((E * N, r), dtype=torch.float16, device=dev),
+            torch.empty((m_all, K), dtype=torch.int8, device=dev),
+            torch.empty((E * N, K), dtype=torch.int8, device=dev),
+            S_e_all.reshape(-1).contiguous(), w1_scale.reshape(-1).contiguous(), by_slot, counts, headers,
+            [syncs[e] for e in range(E)], ctx.pow_target, ctx.pow_key, hits=hits,
+            tile_size_m=config.tile_size_m, tile_size_n=config.tile_size_n, tile_size_k=config.tile_size_k)
+        # out[slot_indices] = C (pearl_moe_experts.py:347) for all experts at once
+        scatter_rows(by_slot, out, layout.slot_indices)
+        for e in range(E):
+            if counts[e]:
+                res.per_expert[e] = MinedGemm(headers[e], syncs[e], ctx.commitment_hash_A,
+                                              ctx.commitment_hash_B, hits[e] if hits else None)
+        return out, res
     for e in range(E):
         start, count = layout.expert_slice(e)
         if count == 0:

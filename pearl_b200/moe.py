@@ -88,3 +88,92 @@ def scatter_rows(src: torch.Tensor, dst: torch.Tensor, indices: torch.Tensor) ->
                            row_bytes=row_bytes)
     with torch.cuda.device(src.device):
         _lib.call("pb2_scatter_rows", p, _stream(src.device), "scatter_rows")
+
+
+def noisy_gemm_grouped(
+    A, B, EAL, EAL_fp16, EBR, EBR_fp16, EAR_R_major, EBL_R_major, EAR_K_major, EBL_K_major,
+    AxEBL_fp16, EARxBpEB_fp16, ApEA, BpEB, A_scales, B_scales, C, expert_rows,
+    host_signal_headers, host_signal_syncs, pow_target, pow_key, *, hits=None, transcripts=None,
+    digests=None, run_noising_A: bool = True, run_noising_B: bool = True, tile_size_m: int = 128,
+    tile_size_n: int = 256, tile_size_k: int = 128,
+):
+    """The mined GEMM1 of every expert of a MoE layer in one call: for expert
+    e, exactly ``noisy_gemm`` (run_noising_A/B, reduction and denoising on) of
+    its rows of A against its rows of B -- the loop of
+    pearl_moe_experts.py:304-343 -- as one noising launch and one persistent
+    mined launch (per 16 experts).
+
+    A-side tensors (A, EAL, EAL_fp16, ApEA, AxEBL_fp16, A_scales, C) hold
+    every expert's rows in expert order, ``expert_rows[e]`` of them for expert
+    e (0 allowed); B-side tensors (B, EBR, EBR_fp16, BpEB, EARxBpEB_fp16,
+    B_scales) hold n rows per expert, expert e at rows [e n, e n + n); the
+    K-side factors EAR_* / EBL_* are shared.  ``host_signal_headers`` /
+    ``host_signal_syncs`` (and the optional ``hits`` / ``transcripts`` /
+    ``digests``) are per-expert lists, used as for that expert's own
+    noisy_gemm."""
+    from .pearl_gemm_interface import _check_matmul_config, _check_tensor, _gemm_params, _ptr
+
+    E = len(expert_rows)
+    if E == 0:
+        _fail("expert_rows must not be empty")
+    m, k = A.shape
+    n_all = B.shape[0]
+    if n_all % E:
+        _fail("B must hold the same number of rows for every expert")
+    n = n_all // E
+    r = EAL.shape[1]
+    if sum(int(v) for v in expert_rows) != m or any(int(v) < 0 for v in expert_rows):
+        _fail(f"expert_rows must be non-negative and add up to A's {m} rows")
+    _check_matmul_config("noisy_gemm", tile_size_m, tile_size_n, tile_size_k, 1, 1, None, r)
+    for t, shape, dt, name in (
+            (A, (m, k), torch.int8, "A"), (EAL, (m, r), torch.int8, "EAL"),
+            (EAL_fp16, (m, r), torch.float16, "EAL_fp16"), (ApEA, (m, k), torch.int8, "ApEA"),
+            (AxEBL_fp16, (m, r), torch.float16, "AxEBL_fp16"), (A_scales, (m,), torch.float32, "A_scales"),
+            (C, (m, n), torch.bfloat16, "C"), (B, (n_all, k), torch.int8, "B"),
+            (EBR, (n_all, r), torch.int8, "EBR"), (EBR_fp16, (n_all, r), torch.float16, "EBR_fp16"),
+            (BpEB, (n_all, k), torch.int8, "BpEB"), (EARxBpEB_fp16, (n_all, r), torch.float16, "EARxBpEB_fp16"),
+            (B_scales, (n_all,), torch.float32, "B_scales"), (EAR_R_major, (k, r), torch.int8, "EAR_R_major"),
+            (EBL_R_major, (k, r), torch.int8, "EBL_R_major"), (EAR_K_major, (r, k), torch.int8, "EAR_K_major"),
+            (EBL_K_major, (r, k), torch.int8, "EBL_K_major")):
+        _check_tensor(t, shape, dt, name)
+    for t, name in ((pow_target, "pow_target"), (pow_key, "pow_key")):
+        _check_tensor(t, (8,), torch.uint32, name)
+    if len(host_signal_headers) != E or len(host_signal_syncs) != E:
+        _fail("one host signal header and one sync buffer per expert")
+    p = _gemm_params(m, n, k, r, _device_index(A), tile_size_m, tile_size_n, tile_size_k, 1, 1, None, None,
+                     True)
+    p.A, p.B, p.EAL, p.EBR = _ptr(A), _ptr(B), _ptr(EAL), _ptr(EBR)
+    p.EAR_R_major, p.EBL_R_major = _ptr(EAR_R_major), _ptr(EBL_R_major)
+    p.EAR_K_major, p.EBL_K_major = _ptr(EAR_K_major), _ptr(EBL_K_major)
+    p.ApEA, p.BpEB = _ptr(ApEA), _ptr(BpEB)
+    p.EAL_fp16, p.EBR_fp16 = _ptr(EAL_fp16), _ptr(EBR_fp16)
+    p.AxEBL_fp16, p.EARxBpEB_fp16 = _ptr(AxEBL_fp16), _ptr(EARxBpEB_fp16)
+    p.A_scales, p.B_scales, p.C = _ptr(A_scales), _ptr(B_scales), _ptr(C)
+    p.pow_target, p.pow_key = _ptr(pow_target), _ptr(pow_key)
+    p.run_noising_a, p.run_noising_b = int(bool(run_noising_A)), int(bool(run_noising_B))
+    p.k_blocks_per_split_noising_a = p.k_blocks_per_split_noising_b = -1
+    table = (_lib.ExpertGemm * E)()
+    row0 = 0
+    for e in range(E):
+        q = table[e]
+        q.m, q.a_row0 = int(expert_rows[e]), row0
+        row0 += int(expert_rows[e])
+        hdr, sync = host_signal_headers[e], host_signal_syncs[e]
+        if q.m > 0:
+            if sync is None or not sync.is_cuda or sync.numel() != _lib.HOST_SIGNAL_SYNC_SIZE:
+                _fail(f"expert {e}: host_signal_sync must be a {_lib.HOST_SIGNAL_SYNC_SIZE}-byte CUDA buffer")
+            if hdr is not None and (hdr.is_cuda or not hdr.is_pinned()):
+                _fail(f"expert {e}: host_signal_header_pinned must be a pinned CPU tensor")
+        q.host_signal_sync = _ptr(sync)
+        q.host_signal_header_pinned = _ptr(hdr)
+        if hits is not None and hits[e] is not None:
+            q.hits, q.hit_capacity = _ptr(hits[e]), hits[e].shape[0]
+        for lst, words, field in ((transcripts, 16, "transcripts"), (digests, 8, "digests")):
+            if lst is not None and lst[e] is not None:
+                _check_tensor(lst[e], ((q.m // 2) * (n // 64), words), (torch.int32, torch.uint32),
+                              f"{field}[{e}]")
+                setattr(q, field, _ptr(lst[e]))
+    g = _lib.GroupedGemmParams()
+    g.shared, g.num_experts, g.experts = p, E, table
+    with torch.cuda.device(A.device):
+        _lib.call("pb2_noisy_gemm_grouped", g, _stream(A.device), "noisy_gemm_grouped")

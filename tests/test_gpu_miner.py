@@ -233,7 +233,8 @@ def test_weight_root_cached_per_job_and_refreshed_after_a_write():
 
 
 # -------------------------------------------------------------- MoE GEMM1 ---
-def test_moe_gemm1_per_expert_parity():
+@pytest.mark.parametrize("grouped", [True, False])
+def test_moe_gemm1_per_expert_parity(grouped):
     E, tokens, top_k, N, K, r = 4, 200, 2, 256, 512, 128
     g = torch.Generator().manual_seed(12)
     A = torch.randint(-64, 64, (tokens, K), generator=g, dtype=torch.int8)
@@ -244,7 +245,7 @@ def test_moe_gemm1_per_expert_parity():
     key, _ = _job(13)
     target = 1 << 251  # ~1 in 32 full hash tiles
     out, res = MN.moe_gemm1(A.cuda(), sa.cuda(), ids.cuda(), w1.cuda(), w1s.cuda(),
-                            MN.MiningJob(key, target, True), hit_capacity=4096)
+                            MN.MiningJob(key, target, True), hit_capacity=4096, grouped=grouped)
     torch.cuda.synchronize()
     # Commitment: roots of A and the stacked weights, routing order and offsets.
     rd, si, off = O.routing_order(ids.numpy(), E)
