@@ -572,6 +572,38 @@ def run_workload(args, world, rank, local):
         return _line(args, world, "16384 x 8192 x 8192 int8 mined GEMM with "
                      "commitment (tensor_hash A,B), noise_gen, noising, transcript, BLAKE3",
                      2.0 * m * n * k, ms, {"m": m, "n": n, "k": k, "r": R}, 1) if rank == 0 else None
+    if args.workload == "fp8_16384":
+        # The FP8 extension of the mined contraction on the 16384 x 8192 x
+        # 8192 shape: normal(0,1) E4M3 operands with per-tensor scales.
+        import pearl_b200 as pg
+        m, n, k = 16384, 8192, 8192
+        gdev = torch.Generator(device=dev).manual_seed(91 + rank)
+        A8 = torch.randn(m, k, generator=gdev, device=dev).to(torch.float8_e4m3fn)
+        B8 = torch.randn(n, k, generator=gdev, device=dev).to(torch.float8_e4m3fn)
+        sa = torch.full((1,), 1 / 16, device=dev)
+        sb = torch.full((1,), 1 / 16, device=dev)
+        C = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+        header, sync = signal_buffers(pg, dev)
+        target = pg.make_pow_target_tensor(target_value(TARGET_FRACTION), dev)
+        keys = [torch.tensor(list(shard.rank_job_key(base, rank, i)), dtype=torch.uint8).to(dev).view(torch.uint32)
+                for i in range(8)]
+
+        def step(i):
+            pg.fp8.mined_gemm_fp8(A8, B8, sa, sb, C, header, sync, target, keys[i % 8])
+        ms = _time_steps(step, args.steps, args.warmup, dev, world)
+        if rank != 0:
+            return None
+        line = _line(args, world, "FP8 E4M3 mined GEMM M=16384 N=K=8192 (per-tensor scales, transcript over "
+                     "f32 accumulators, BLAKE3, target compare; no noise)", 2.0 * m * n * k, ms,
+                     {"m": m, "n": n, "k": k, "r": R, "operands": "float8_e4m3fn normal(0,1)"}, 1)
+        line["dtype"] = "fp8_e4m3"
+        line["metric"] = "effective TFLOPS (mined FP8 E4M3 GEMM with fused transcript hashing)"
+        line["unit"] = "TFLOPS"
+        line["roofline"] = {"kernel": "noisy_gemm_kernel<kind::f8f6f4>", "bound": "tensor",
+                            "achieved": line["value"], "peak": round(2.0 * measured_peaks()["bf16_tflops"], 1),
+                            "unit": "TFLOPS", "frac": round(line["value"] / (2.0 * measured_peaks()["bf16_tflops"]), 4),
+                            "peak_source": "2 x measured burst bf16 (B200 dense FP8 = 2 x bf16)", "traffic": None}
+        return line
     if args.workload in ("llama", "llama_decode"):
         tokens = 8192 if args.workload == "llama" else 256
         hidden, mlp, layers = 4096, 14336, 32
@@ -664,7 +696,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--ref-budget", type=float, default=90.0)
     ap.add_argument("--workload", default="gemm8192",
-                    choices=["gemm8192", "gemm16384", "llama", "llama_decode", "moe"],
+                    choices=["gemm8192", "gemm16384", "llama", "llama_decode", "moe", "fp8_16384"],
                     help="gemm8192 (default) is the headline GEMM; the others are the larger "
                          "configs 3-5 measured through the miner-facing operators")
     ap.add_argument("--k", type=int, default=8192,

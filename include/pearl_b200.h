@@ -373,6 +373,46 @@ PB2_API int pb2_noisy_gemm(const pb2_gemm_params* p, void* stream);
  * operands from p->ApEA / p->BpEB (the reference passes A and B there). */
 PB2_API int pb2_gemm(const pb2_gemm_params* p, void* stream);
 
+/* ------------------------------------------------------ FP8 mined GEMM ---
+ * No reference counterpart: the protocol defines mined GEMMs of 7-bit
+ * integers only (zk-pow/src/api/proof.rs:23-25), and the reference's only
+ * FP8 GEMM is the un-mined MoE GEMM2 (pearl_moe_experts.py:377-434).  This
+ * is the same mined GEMM on FP8 operands (both E4M3 or both E5M2) with
+ * per-tensor scales:
+ *   S = A . B^T accumulated in f32 on the tensor cores (kind::f8f6f4),
+ * the transcript of every 2 x 64 hash tile folded from the f32 accumulator
+ * BIT PATTERNS every r = 128 steps of k exactly as the int8 path folds its
+ * int32 words, keyed BLAKE3 (pow_key) and the target compare, hits as for
+ * pb2_noisy_gemm, and C = bf16(S * A_scale[0] * B_scale[0]).  No noise and
+ * no denoise terms.  The f32 accumulation order inside the tensor core is
+ * not specified, so the transcript is reproducible off the device only
+ * where every partial sum is exact (integer-valued operands with
+ * |partial sums| < 2^24).  Same shape rules as pb2_noisy_gemm (k % 128 == 0,
+ * n % 8 == 0, dumps need m % 16 == 0 and n % 256 == 0); A, B, C 16-byte
+ * aligned; the scales are one float each on `device`. */
+#define PB2_FP8_E4M3 0
+#define PB2_FP8_E5M2 1
+typedef struct pb2_fp8_gemm_params {
+  int device;
+  int64_t m, n, k, r;    /* r: transcript period, 128 */
+  const void* A;         /* (m,k) FP8 */
+  const void* B;         /* (n,k) FP8 */
+  int format;            /* PB2_FP8_E4M3 or PB2_FP8_E5M2 (both operands) */
+  const float* A_scale;  /* 1 float */
+  const float* B_scale;  /* 1 float */
+  void* C;               /* (m,n) bf16 */
+  void* host_signal_header_pinned;
+  void* host_signal_sync;
+  const uint32_t* pow_target;
+  const uint32_t* pow_key;
+  int skip_reduction;
+  uint32_t* hits;
+  int64_t hit_capacity;
+  uint32_t* transcripts;
+  uint32_t* digests;
+} pb2_fp8_gemm_params;
+PB2_API int pb2_mined_gemm_fp8(const pb2_fp8_gemm_params* p, void* stream);
+
 /* ---------------------------------------------------- grouped noisy_gemm ---
  * Replaces the per-expert loop of the mined MoE GEMM1
  * (miner/vllm-miner/src/vllm_miner/pearl_moe_experts.py:304-343, each pass a

@@ -50,6 +50,7 @@ def lib():
         L.po_jackpot_hash.argtypes = [u32p, u8p, u32p]
         L.po_u256_le.argtypes = [u32p, u32p]
         L.po_mine_tiles.argtypes = [i8p, i8p, i64, i64, i64, i64, u8p, u32p, i64, i64, u32p, u32p, u8p]
+        L.po_mine_tiles_f32.argtypes = L.po_mine_tiles.argtypes
         L.po_hash_activations.argtypes = [u8p, u8p, u32p, i64, u8p, u8p]
         L.po_commitment.argtypes = [u8p, u8p, u8p, ctypes.c_int, ctypes.c_uint32, ctypes.c_uint32,
                                     u8p, u32p, i64, u8p, u8p]
@@ -190,10 +191,12 @@ class MineResult:
 
 
 def mine_tiles(ap: np.ndarray, bp: np.ndarray, r: int, key: bytes, target: int,
-               tile_begin: int = 0, tile_end: int | None = None) -> MineResult:
+               tile_begin: int = 0, tile_end: int | None = None, acc_f32: bool = False) -> MineResult:
     """Transcripts, digests and hit flags of protocol hash tiles
     [tile_begin, tile_end) for noised operands ap (m x k) and bp (n x k)
-    (zk-pow/src/ffi/mine.rs:86-110)."""
+    (zk-pow/src/ffi/mine.rs:86-110).  acc_f32 folds the float32 bit patterns
+    of the accumulators instead of their int32 words (the FP8 mined GEMM of
+    this build; exact for integer-valued operands while |sums| < 2^24)."""
     ap = np.ascontiguousarray(ap, np.int8)
     bp = np.ascontiguousarray(bp, np.int8)
     m, k = ap.shape
@@ -206,9 +209,10 @@ def mine_tiles(ap: np.ndarray, bp: np.ndarray, r: int, key: bytes, target: int,
     dg = np.zeros((cnt, 8), np.uint32)
     hits = np.zeros(cnt, np.uint8)
     tw = target_words(target)
-    lib().po_mine_tiles(_p(ap, ctypes.c_int8), _p(bp, ctypes.c_int8), m, n, k, r,
-                        _p(_bytes32(key), ctypes.c_uint8), _p(tw, ctypes.c_uint32), tile_begin, tile_end,
-                        _p(tr, ctypes.c_uint32), _p(dg, ctypes.c_uint32), _p(hits, ctypes.c_uint8))
+    fn = lib().po_mine_tiles_f32 if acc_f32 else lib().po_mine_tiles
+    fn(_p(ap, ctypes.c_int8), _p(bp, ctypes.c_int8), m, n, k, r, _p(_bytes32(key), ctypes.c_uint8),
+       _p(tw, ctypes.c_uint32), tile_begin, tile_end, _p(tr, ctypes.c_uint32), _p(dg, ctypes.c_uint32),
+       _p(hits, ctypes.c_uint8))
     return MineResult(tr, dg, hits.astype(bool), tile_begin)
 
 

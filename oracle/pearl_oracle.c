@@ -312,10 +312,20 @@ static inline uint32_t rotl32(uint32_t x, int n) {
   return (x << n) | (x >> (32 - n));
 }
 
-/* One hash tile given explicit row and column index lists (h rows, w cols). */
-PO_EXPORT void po_jackpot_tile(const int8_t* ap, const int8_t* bp, int64_t k,
-                               int64_t r, const int64_t* rows, int h,
-                               const int64_t* cols, int w, uint32_t out[16]) {
+static inline uint32_t f32_bits(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  return u;
+}
+
+/* One hash tile given explicit row and column index lists (h rows, w cols).
+ * acc_f32 != 0: the words folded are the float32 bit patterns of the
+ * accumulators (this build's FP8 mined GEMM accumulates in f32; exact, and
+ * so order-independent, only while every partial sum stays below 2^24). */
+static void jackpot_tile_mode(const int8_t* ap, const int8_t* bp, int64_t k,
+                              int64_t r, const int64_t* rows, int h,
+                              const int64_t* cols, int w, int acc_f32,
+                              uint32_t out[16]) {
   int32_t acc[2 * 64];
   int32_t* accp = acc;
   int32_t* heap = NULL;
@@ -336,7 +346,7 @@ PO_EXPORT void po_jackpot_tile(const int8_t* ap, const int8_t* bp, int64_t k,
         int32_t s = 0;
         for (int64_t l = ll - r; l < ll; ++l) s += (int32_t)arow[l] * (int32_t)brow[l];
         accp[u * w + v] += s;
-        x ^= (uint32_t)accp[u * w + v];
+        x ^= acc_f32 ? f32_bits((float)accp[u * w + v]) : (uint32_t)accp[u * w + v];
       }
     }
     int tid = (int)((ll / r - 1) % 16);
@@ -344,6 +354,12 @@ PO_EXPORT void po_jackpot_tile(const int8_t* ap, const int8_t* bp, int64_t k,
   }
   memcpy(out, t, sizeof(t));
   free(heap);
+}
+
+PO_EXPORT void po_jackpot_tile(const int8_t* ap, const int8_t* bp, int64_t k,
+                               int64_t r, const int64_t* rows, int h,
+                               const int64_t* cols, int w, uint32_t out[16]) {
+  jackpot_tile_mode(ap, bp, k, r, rows, h, cols, w, 0, out);
 }
 
 /* Jackpot hash (zk-pow/src/api/proof_utils.rs:1511-1514): keyed BLAKE3 of
@@ -371,13 +387,11 @@ PO_EXPORT int po_u256_le(const uint32_t a[8], const uint32_t b[8]) {
  * threads_partition requires).  Tile index = t_row * (n/64) + t_col where
  * t_row in [0, m/2) and t_col in [0, n/64).  Writes transcripts (16 words),
  * digests (8 words) and hit flags for tiles [tile_begin, tile_end). */
-PO_EXPORT void po_mine_tiles(const int8_t* ap, const int8_t* bp, int64_t m,
-                             int64_t n, int64_t k, int64_t r,
-                             const uint8_t key[32], const uint32_t target[8],
-                             int64_t tile_begin, int64_t tile_end,
-                             uint32_t* transcripts, uint32_t* digests,
-                             uint8_t* hits) {
-  (void)m;
+static void mine_tiles_mode(const int8_t* ap, const int8_t* bp, int64_t n,
+                            int64_t k, int64_t r, const uint8_t key[32],
+                            const uint32_t target[8], int64_t tile_begin,
+                            int64_t tile_end, int acc_f32, uint32_t* transcripts,
+                            uint32_t* digests, uint8_t* hits) {
   int64_t tcols = n / 64;
 #pragma omp parallel for schedule(dynamic, 16)
   for (int64_t t = tile_begin; t < tile_end; ++t) {
@@ -391,13 +405,35 @@ PO_EXPORT void po_mine_tiles(const int8_t* ap, const int8_t* bp, int64_t m,
       cols[2 * j + 1] = ocol + 8 * j + 1;
     }
     uint32_t tr[16], dg[8];
-    po_jackpot_tile(ap, bp, k, r, rows, 2, cols, 64, tr);
+    jackpot_tile_mode(ap, bp, k, r, rows, 2, cols, 64, acc_f32, tr);
     po_jackpot_hash(tr, key, dg);
     int64_t slot = t - tile_begin;
     if (transcripts) memcpy(transcripts + 16 * slot, tr, sizeof(tr));
     if (digests) memcpy(digests + 8 * slot, dg, sizeof(dg));
     if (hits) hits[slot] = (uint8_t)po_u256_le(dg, target);
   }
+}
+
+PO_EXPORT void po_mine_tiles(const int8_t* ap, const int8_t* bp, int64_t m,
+                             int64_t n, int64_t k, int64_t r,
+                             const uint8_t key[32], const uint32_t target[8],
+                             int64_t tile_begin, int64_t tile_end,
+                             uint32_t* transcripts, uint32_t* digests,
+                             uint8_t* hits) {
+  (void)m;
+  mine_tiles_mode(ap, bp, n, k, r, key, target, tile_begin, tile_end, 0, transcripts, digests, hits);
+}
+
+/* po_mine_tiles over the float32 bit patterns of the accumulators (see
+ * jackpot_tile_mode): the operands are the integer values of FP8 elements. */
+PO_EXPORT void po_mine_tiles_f32(const int8_t* ap, const int8_t* bp, int64_t m,
+                                 int64_t n, int64_t k, int64_t r,
+                                 const uint8_t key[32], const uint32_t target[8],
+                                 int64_t tile_begin, int64_t tile_end,
+                                 uint32_t* transcripts, uint32_t* digests,
+                                 uint8_t* hits) {
+  (void)m;
+  mine_tiles_mode(ap, bp, n, k, r, key, target, tile_begin, tile_end, 1, transcripts, digests, hits);
 }
 
 /* ------------------------------------------------------------------------- */

@@ -41,6 +41,7 @@ from .pearl_gemm_interface import (
 from . import moe
 from . import quantization
 from . import device_waits
+from . import fp8
 from . import ops  # noqa: F401  (registers torch.ops.pearl_gemm.*)
 
 __all__ = [
@@ -62,6 +63,7 @@ __all__ = [
     "moe",
     "quantization",
     "device_waits",
+    "fp8",
     "kEALScaleFactorDenoise",
     "kEBRScaleFactorDenoise",
     "make_pow_target_tensor",

@@ -35,7 +35,7 @@ EXPORTED = [
     "pb2_commitment_hash_from_merkle_roots", "pb2_build_routing_data",
     "pb2_build_routing_data_scratchpad_bytes", "pb2_quantize", "pb2_scatter_rows",
     "pb2_merkle_layers", "pb2_merkle_nodes", "pb2_set_wait_budget_cycles", "pb2_wait_selftest",
-    "pb2_rcp_approx_f32", "pb2_noisy_gemm_grouped",
+    "pb2_rcp_approx_f32", "pb2_noisy_gemm_grouped", "pb2_mined_gemm_fp8",
 ]
 DEFAULT_WAIT_BUDGET_CYCLES = 2000000000
 
@@ -81,6 +81,14 @@ class GemmParams(ctypes.Structure):
                 ("skip_reduction", ctypes.c_int), ("skip_denoising", ctypes.c_int),
                 ("inner_hash_counter", _vp), ("enable_debug", ctypes.c_int),
                 ("hits", _vp), ("hit_capacity", _i64), ("transcripts", _vp), ("digests", _vp)]
+
+
+class Fp8GemmParams(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int), ("m", _i64), ("n", _i64), ("k", _i64), ("r", _i64), ("A", _vp),
+                ("B", _vp), ("format", ctypes.c_int), ("A_scale", _vp), ("B_scale", _vp), ("C", _vp),
+                ("host_signal_header_pinned", _vp), ("host_signal_sync", _vp), ("pow_target", _vp),
+                ("pow_key", _vp), ("skip_reduction", ctypes.c_int), ("hits", _vp), ("hit_capacity", _i64),
+                ("transcripts", _vp), ("digests", _vp)]
 
 
 class ExpertGemm(ctypes.Structure):
@@ -145,6 +153,7 @@ def load() -> ctypes.CDLL:
         L = ctypes.CDLL(LIB_PATH)
         for name in ("pb2_noise_gen", "pb2_noise_A", "pb2_noise_B", "pb2_denoise_converter",
                      "pb2_noisy_gemm", "pb2_gemm", "pb2_noisy_gemm_static_scratch", "pb2_noisy_gemm_grouped",
+                     "pb2_mined_gemm_fp8",
                      "pb2_tensor_hash", "pb2_commitment_hash_from_merkle_roots",
                      "pb2_build_routing_data", "pb2_quantize", "pb2_scatter_rows", "pb2_merkle_layers"):
             getattr(L, name).restype = ctypes.c_int

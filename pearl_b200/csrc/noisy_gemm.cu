@@ -65,6 +65,7 @@ struct MainArgs {
   int N, K, R;               // N: columns of C (rows of B per problem)
   int tiles_n, num_tiles, group;
   int tpr;  // tiles a CTA pair runs per round: 2 (two TMEM slots in alternation) or 1
+  int scale_per_tensor;  // sA[0] and sB[0] scale every row and column (FP8 operands)
   SignalSync* sync;  // where a timed-out wait records its error
   const uint32_t* target;
   const uint32_t* key;
@@ -224,9 +225,14 @@ __device__ void publish_hit(const MainArgs& a, const ExpertEntry& E, int tm128, 
 //
 // kE = problems per launch: 1, or up to kMaxExperts (the grouped MoE GEMM:
 // every expert's tiles in one persistent launch, x.ex[e] per expert).
-template <int BK, int kSPU, bool kReduce, bool kDenoise, bool kDebug, int kTN, int kE>
+//
+// kKind = operand type: 0 = int8 (kind::i8, int32 accumulators), 1 = FP8
+// E4M3, 2 = FP8 E5M2 (kind::f8f6f4, f32 accumulators whose bit patterns the
+// transcript folds; no noising or denoise terms).
+template <int BK, int kSPU, bool kReduce, bool kDenoise, bool kDebug, int kTN, int kE, int kKind = 0>
 __global__ void __launch_bounds__(kThreads, 1)
     noisy_gemm_kernel(const __grid_constant__ MainArgs a, const __grid_constant__ ExpertTable<kE> x) {
+  static_assert(kKind == 0 || !kDenoise, "FP8 operands carry no denoise terms");
   static_assert(kTN == BN || (kTN == BN / 2 && !kReduce && !kDenoise), "narrow tiles: plain GEMM only");
   constexpr int kAStage = BMC * BK;        // this CTA's 128 rows of A
   constexpr int kBStage = (kTN / 2) * BK;  // this CTA's half of the tile's rows of B
@@ -236,7 +242,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       (kStageBudget / kStageBytes) < kMaxStages ? (kStageBudget / kStageBytes) : kMaxStages;
   static_assert(kStageBudget + (kReduce ? kXbufBytes : 0) + kCStageBytes + 1024 + 256 <= 232448,
                 "shared memory plan exceeds 227 KB");
-  constexpr uint32_t kIdescI8 = idesc_i8(BM, kTN);
+  constexpr uint32_t kIdescI8 =
+      kKind == 0 ? idesc_i8(BM, kTN) : idesc_f8(BM, kTN, uint32_t(kKind - 1), uint32_t(kKind - 1));
   constexpr uint32_t kIdescF16 = idesc_f16(BM, BN);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -422,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint64_t ad = sdesc_kmajor<BK>(sbase + j * kStageBytes);
           const uint64_t bd = sdesc_kmajor<BK>(sbase + j * kStageBytes + kAStage);
-          umma_i8_2sm_stage_warp<BK / 32>(dt, ad, bd, kIdescI8, uint32_t((u | st) != 0), &S.empty[j], kPairMask);
+          umma_8bit_2sm_stage_warp<BK / 32, (kKind != 0)>(dt, ad, bd, kIdescI8, uint32_t((u | st) != 0), &S.empty[j], kPairMask);
         }
         // With the transcript every unit is a fold event, and the stage's
         // commit above doubles as "accumulator ready" (one commit per unit
@@ -612,9 +619,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       float2 sbv = make_float2(0.f, 0.f);
       if (do_store) {  // scales first: their latency overlaps the loads
         const int row = tm * BM + int(rank) * BMC + 32 * q + lane;
-        rs = (row < E.m ? E.sA[row] : 0.0f) * (is_main ? 1.0f : 4096.0f);
+        rs = (row < E.m ? E.sA[a.scale_per_tensor ? 0 : row] : 0.0f) * (is_main ? 1.0f : 4096.0f);
         const int c = tn * kTN + 64 * wi + 2 * lane;  // this lane's two column scales
-        if (c < a.N) sbv = *reinterpret_cast<const float2*>(E.sB + c);
+        if (c < a.N)
+          sbv = a.scale_per_tensor ? make_float2(E.sB[0], E.sB[0]) : *reinterpret_cast<const float2*>(E.sB + c);
       }
       const int row0 = tm * BM + int(rank) * BMC + 32 * q;
       uint8_t* box = cstage + fw * kCBoxBytes;
@@ -642,8 +650,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int src = 16 * h + i / 2;  // lane holding columns 32h + i, +1
             const float bx = __shfl_sync(0xffffffffu, sbv.x, src);
             const float by = __shfl_sync(0xffffffffu, sbv.y, src);
-            const float f0 = is_main ? float(int(v[i])) : __uint_as_float(v[i]);
-            const float f1 = is_main ? float(int(v[i + 1])) : __uint_as_float(v[i + 1]);
+            const float f0 = (is_main && kKind == 0) ? float(int(v[i])) : __uint_as_float(v[i]);
+            const float f1 = (is_main && kKind == 0) ? float(int(v[i + 1])) : __uint_as_float(v[i + 1]);
             packed[i / 2] = pack_bf16(f0 * rs * bx, f1 * rs * by);
           }
           store_c_packed(&E.tmC, box, packed, row0, tn * kTN + 64 * wi + 32 * h, lane);
@@ -744,9 +752,9 @@ int& resident_pairs(int device) {
   return cached[device & 63];
 }
 
-template <int BK, int SPU, bool R_, bool D_, bool G_, int TN, int kE>
+template <int BK, int SPU, bool R_, bool D_, bool G_, int TN, int kE, int kKind = 0>
 int launch_variant(const MainArgs& a, const ExpertTable<kE>& x, int device, cudaStream_t s) {
-  auto kern = noisy_gemm_kernel<BK, SPU, R_, D_, G_, TN, kE>;
+  auto kern = noisy_gemm_kernel<BK, SPU, R_, D_, G_, TN, kE, kKind>;
   const int smem = stage_budget(R_) + (R_ ? kXbufBytes : 0) + kCStageBytes + int(sizeof(Smem)) + 1024;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return launch_status();
@@ -1096,4 +1104,65 @@ extern "C" int pb2_noisy_gemm_grouped(const pb2_grouped_gemm_params* gp, void* s
     if ((st = pb2_noise_B(&qb, stream))) return st;
   }
   return run_grouped_kernel(p, gp->experts, E, s);
+}
+
+namespace pb2 {
+namespace {
+template <int kKind>
+int launch_fp8(const MainArgs& a, const ExpertTable<1>& x, int device, bool reduce, cudaStream_t s) {
+  return reduce ? launch_variant<128, 1, true, false, false, BN, 1, kKind>(a, x, device, s)
+                : launch_variant<128, 1, false, false, false, BN, 1, kKind>(a, x, device, s);
+}
+}  // namespace
+}  // namespace pb2
+
+extern "C" int pb2_mined_gemm_fp8(const pb2_fp8_gemm_params* pp, void* stream) {
+  using namespace pb2;
+  if (!pp) return PB2_ERR_INVALID_ARGUMENT;
+  const pb2_fp8_gemm_params& f = *pp;
+  const bool reduce = !f.skip_reduction;
+  if (f.format != PB2_FP8_E4M3 && f.format != PB2_FP8_E5M2) return PB2_ERR_UNSUPPORTED_CONFIG;
+  if (f.r != 128) return PB2_ERR_UNSUPPORTED_CONFIG;
+  // The same shape, pointer and buffer rules as the int8 mined GEMM.
+  pb2_gemm_params q{};
+  q.device = f.device;
+  q.m = f.m; q.n = f.n; q.k = f.k; q.r = f.r;
+  q.ApEA = const_cast<int8_t*>(static_cast<const int8_t*>(f.A));
+  q.BpEB = const_cast<int8_t*>(static_cast<const int8_t*>(f.B));
+  q.A_scales = f.A_scale;
+  q.B_scales = f.B_scale;
+  q.C = f.C;
+  q.host_signal_header_pinned = f.host_signal_header_pinned;
+  q.host_signal_sync = f.host_signal_sync;
+  q.pow_target = f.pow_target;
+  q.pow_key = f.pow_key;
+  q.tile_size_m = BMC; q.tile_size_n = BN; q.tile_size_k = kTileK;
+  q.cluster_size_m = q.cluster_size_n = 1;
+  q.hits = f.hits; q.hit_capacity = f.hit_capacity;
+  q.transcripts = f.transcripts; q.digests = f.digests;
+  int st = check_main_args(q, reduce, false);
+  if (st) return st;
+  if ((st = set_device(f.device))) return st;
+  MainArgs a;
+  std::memset(&a, 0, sizeof(a));
+  ExpertTable<1> x;
+  std::memset(&x, 0, sizeof(x));
+  if ((st = make_shared_args(a, q, 128, BN, false))) return st;
+  if ((st = make_entry(x.ex[0], q.ApEA, nullptr, nullptr, f.A_scale, f.C, f.m, f.n, f.k, f.r, 128, false)))
+    return st;
+  x.count = 1;
+  ExpertEntry& e = x.ex[0];
+  e.sB = f.B_scale;
+  e.sync = static_cast<SignalSync*>(f.host_signal_sync);
+  e.header = static_cast<SignalHeader*>(f.host_signal_header_pinned);
+  e.hits = f.hits;
+  e.hit_cap = f.hits ? f.hit_capacity : 0;
+  e.transcripts = f.transcripts;
+  e.digests = f.digests;
+  a.num_tiles = e.tiles_m * a.tiles_n;
+  a.tpr = 2;
+  a.scale_per_tensor = 1;
+  a.sync = e.sync;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return f.format == PB2_FP8_E4M3 ? launch_fp8<1>(a, x, f.device, reduce, s) : launch_fp8<2>(a, x, f.device, reduce, s);
 }

@@ -465,40 +465,64 @@ __device__ __forceinline__ void umma_commit_2sm_warp(uint64_t* bar, uint16_t cta
 // `cta_mask`.  One election and one predicated block per stage keep the
 // issuing warp's instruction count low; it shares its sub-partition (and
 // that sub-partition's tcgen05 instruction path) with fold warps.
-template <int kSteps>
-__device__ __forceinline__ void umma_i8_2sm_stage_warp(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                                       uint32_t idesc, uint32_t accumulate, uint64_t* bar,
-                                                       uint16_t cta_mask) {
+#define PB2_STAGE4(KIND)                                                                                \
+  asm volatile(                                                                                        \
+      "{\n\t.reg .pred e, p;\n\t"                                                                     \
+      "elect.sync _|e, 0xffffffff;\n\t"                                                                \
+      "setp.ne.b32 p, %4, 0;\n\t"                                                                      \
+      "@e tcgen05.mma.cta_group::2.kind::" KIND " [%0], %1, %2, %3, p;\n\t"                             \
+      "setp.eq.u32 p, %4, %4;\n\t"                                                                     \
+      "@e tcgen05.mma.cta_group::2.kind::" KIND " [%0], %5, %6, %3, p;\n\t"                             \
+      "@e tcgen05.mma.cta_group::2.kind::" KIND " [%0], %7, %8, %3, p;\n\t"                             \
+      "@e tcgen05.mma.cta_group::2.kind::" KIND " [%0], %9, %10, %3, p;\n\t"                            \
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"      \
+      " [%11], %12;\n\t}" ::"r"(d_tmem),                                                               \
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "l"(adesc + 2), "l"(bdesc + 2), "l"(adesc + 4), \
+      "l"(bdesc + 4), "l"(adesc + 6), "l"(bdesc + 6), "r"(smem_u32(bar)), "h"(cta_mask)                  \
+      : "memory")
+#define PB2_STAGE2(KIND)                                                                                \
+  asm volatile(                                                                                        \
+      "{\n\t.reg .pred e, p;\n\t"                                                                     \
+      "elect.sync _|e, 0xffffffff;\n\t"                                                                \
+      "setp.ne.b32 p, %4, 0;\n\t"                                                                      \
+      "@e tcgen05.mma.cta_group::2.kind::" KIND " [%0], %1, %2, %3, p;\n\t"                             \
+      "setp.eq.u32 p, %4, %4;\n\t"                                                                     \
+      "@e tcgen05.mma.cta_group::2.kind::" KIND " [%0], %5, %6, %3, p;\n\t"                             \
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"      \
+      " [%7], %8;\n\t}" ::"r"(d_tmem),                                                                 \
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "l"(adesc + 2), "l"(bdesc + 2),               \
+      "r"(smem_u32(bar)), "h"(cta_mask)                                                                  \
+      : "memory")
+
+// One operand stage of 2-SM MMAs on 8-bit operands and the stage's commit
+// from ONE elected lane: kSteps MMAs along K (32 bytes each; the first
+// accumulates only if `accumulate`), then a commit of all of them to `bar`
+// in every CTA of `cta_mask`.  kF8 selects kind::f8f6f4 (FP8 operands,
+// f32 accumulators; formats in `idesc`) instead of kind::i8.  One election
+// and one predicated block per stage keep the issuing warp's instruction
+// count low; it shares its sub-partition with fold warps.
+template <int kSteps, bool kF8>
+__device__ __forceinline__ void umma_8bit_2sm_stage_warp(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                                         uint32_t idesc, uint32_t accumulate, uint64_t* bar,
+                                                         uint16_t cta_mask) {
   static_assert(kSteps == 2 || kSteps == 4, "K steps per stage");
-  if constexpr (kSteps == 4) {
-    asm volatile(
-        "{\n\t.reg .pred e, p;\n\t"
-        "elect.sync _|e, 0xffffffff;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "@e tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t"
-        "setp.eq.u32 p, %4, %4;\n\t"
-        "@e tcgen05.mma.cta_group::2.kind::i8 [%0], %5, %6, %3, p;\n\t"
-        "@e tcgen05.mma.cta_group::2.kind::i8 [%0], %7, %8, %3, p;\n\t"
-        "@e tcgen05.mma.cta_group::2.kind::i8 [%0], %9, %10, %3, p;\n\t"
-        "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-        " [%11], %12;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "l"(adesc + 2), "l"(bdesc + 2), "l"(adesc + 4),
-        "l"(bdesc + 4), "l"(adesc + 6), "l"(bdesc + 6), "r"(smem_u32(bar)), "h"(cta_mask)
-        : "memory");
+  if constexpr (kSteps == 4 && kF8) {
+    PB2_STAGE4("f8f6f4");
+  } else if constexpr (kSteps == 4) {
+    PB2_STAGE4("i8");
+  } else if constexpr (kF8) {
+    PB2_STAGE2("f8f6f4");
   } else {
-    asm volatile(
-        "{\n\t.reg .pred e, p;\n\t"
-        "elect.sync _|e, 0xffffffff;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "@e tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t"
-        "setp.eq.u32 p, %4, %4;\n\t"
-        "@e tcgen05.mma.cta_group::2.kind::i8 [%0], %5, %6, %3, p;\n\t"
-        "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-        " [%7], %8;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "l"(adesc + 2), "l"(bdesc + 2),
-        "r"(smem_u32(bar)), "h"(cta_mask)
-        : "memory");
+    PB2_STAGE2("i8");
   }
+}
+#undef PB2_STAGE4
+#undef PB2_STAGE2
+
+// Instruction descriptor of kind::f8f6f4 with FP8 operands and f32
+// accumulators: operand formats E4M3 = 0, E5M2 = 1 (K-major A and B).
+__host__ __device__ constexpr uint32_t idesc_f8(int m, int n, uint32_t afmt, uint32_t bfmt) {
+  return (1u << 4) | (afmt << 7) | (bfmt << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
 }
 
 // 2-D tiled load into this CTA's shared memory whose transaction bytes are

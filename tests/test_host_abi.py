@@ -59,7 +59,9 @@ def _c_sizeof(struct: str) -> int:
     ("pb2_denoise_converter_params", "DenoiseConverterParams"), ("pb2_gemm_params", "GemmParams"),
     ("pb2_tensor_hash_params", "TensorHashParams"), ("pb2_commitment_params", "CommitmentParams"),
     ("pb2_routing_params", "RoutingParams"), ("pb2_quant_params", "QuantParams"),
-    ("pb2_scatter_params", "ScatterParams"), ("pb2_merkle_params", "MerkleParams")])
+    ("pb2_scatter_params", "ScatterParams"), ("pb2_merkle_params", "MerkleParams"),
+    ("pb2_fp8_gemm_params", "Fp8GemmParams"), ("pb2_expert_gemm", "ExpertGemm"),
+    ("pb2_grouped_gemm_params", "GroupedGemmParams")])
 def test_param_struct_layout_matches_header(cname, pyname):
     assert _c_sizeof(cname) == ctypes.sizeof(getattr(_lib, pyname))
 
