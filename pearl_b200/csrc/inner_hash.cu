@@ -23,6 +23,7 @@ __global__ void inner_hash_kernel(const uint32_t* __restrict__ in, int n, uint32
 
 extern "C" int pb2_inner_hash(int device, const uint32_t* in, int64_t n, uint32_t* out,
                               int64_t iterations, void* stream) {
+  pb2::NvtxRange nvtx_range("pb2_inner_hash");
   using namespace pb2;
   if (!in || !out) return PB2_ERR_INVALID_ARGUMENT;
   if (!(n == 64 || n == 96 || n == 128 || n == 192 || n == 256)) return PB2_ERR_INVALID_ARGUMENT;

@@ -185,6 +185,7 @@ bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0;
 }  // namespace pb2
 
 extern "C" int pb2_noise_gen(const pb2_noise_gen_params* pp, void* stream) {
+  pb2::NvtxRange nvtx_range("pb2_noise_gen");
   using namespace pb2;
   if (!pp) return PB2_ERR_INVALID_ARGUMENT;
   const pb2_noise_gen_params& p = *pp;

@@ -675,21 +675,25 @@ int denoise_convert(const int32_t* in, void* out, int64_t count, float scale, cu
 }  // namespace pb2
 
 extern "C" int pb2_noise_A(const pb2_noising_params* p, void* stream) {
+  pb2::NvtxRange nvtx_range("pb2_noise_A");
   if (!p) return PB2_ERR_INVALID_ARGUMENT;
   return pb2::run_noising(*p, false, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int pb2_noise_B(const pb2_noising_params* p, void* stream) {
+  pb2::NvtxRange nvtx_range("pb2_noise_B");
   if (!p) return PB2_ERR_INVALID_ARGUMENT;
   return pb2::run_noising(*p, true, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int pb2_noise_AB(const pb2_noising_params* a, const pb2_noising_params* b, void* stream) {
+  pb2::NvtxRange nvtx_range("pb2_noise_AB");
   if (!a || !b) return PB2_ERR_INVALID_ARGUMENT;
   return pb2::run_noising_both(*a, *b, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int pb2_denoise_converter(const pb2_denoise_converter_params* pp, void* stream) {
+  pb2::NvtxRange nvtx_range("pb2_denoise_converter");
   using namespace pb2;
   if (!pp) return PB2_ERR_INVALID_ARGUMENT;
   const auto& p = *pp;

@@ -1001,6 +1001,7 @@ int run_noising_both(const pb2_noising_params& pa, const pb2_noising_params& pb,
 }  // namespace pb2
 
 extern "C" int pb2_noisy_gemm(const pb2_gemm_params* pp, void* stream) {
+  pb2::NvtxRange nvtx_range("pb2_noisy_gemm");
   using namespace pb2;
   if (!pp) return PB2_ERR_INVALID_ARGUMENT;
   const pb2_gemm_params& p = *pp;
@@ -1047,6 +1048,7 @@ extern "C" int pb2_noisy_gemm(const pb2_gemm_params* pp, void* stream) {
 }
 
 extern "C" int pb2_gemm(const pb2_gemm_params* pp, void* stream) {
+  pb2::NvtxRange nvtx_range("pb2_gemm");
   using namespace pb2;
   if (!pp) return PB2_ERR_INVALID_ARGUMENT;
   int st = set_device(pp->device);
@@ -1055,6 +1057,7 @@ extern "C" int pb2_gemm(const pb2_gemm_params* pp, void* stream) {
 }
 
 extern "C" int pb2_noisy_gemm_grouped(const pb2_grouped_gemm_params* gp, void* stream) {
+  pb2::NvtxRange nvtx_range("pb2_noisy_gemm_grouped");
   using namespace pb2;
   if (!gp || !gp->experts || gp->num_experts <= 0) return PB2_ERR_INVALID_ARGUMENT;
   const pb2_gemm_params& p = gp->shared;
@@ -1117,6 +1120,7 @@ int launch_fp8(const MainArgs& a, const ExpertTable<1>& x, int device, bool redu
 }  // namespace pb2
 
 extern "C" int pb2_mined_gemm_fp8(const pb2_fp8_gemm_params* pp, void* stream) {
+  pb2::NvtxRange nvtx_range("pb2_mined_gemm_fp8");
   using namespace pb2;
   if (!pp) return PB2_ERR_INVALID_ARGUMENT;
   const pb2_fp8_gemm_params& f = *pp;

@@ -53,6 +53,7 @@ int scratch_on(int device, int32_t** out) {
 }  // namespace
 
 extern "C" int pb2_noisy_gemm_static_scratch(const pb2_gemm_params* pp, void* stream) {
+  pb2::NvtxRange nvtx_range("pb2_noisy_gemm_static_scratch");
   if (!pp) return PB2_ERR_INVALID_ARGUMENT;
   const pb2_gemm_params& p = *pp;
   // The int32 projections live in the library's array, never in the caller's.

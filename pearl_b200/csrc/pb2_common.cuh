@@ -761,6 +761,17 @@ __device__ __forceinline__ uint32_t rotl13(uint32_t x) { return __funnelshift_l(
 
 // Host helpers (pb2_host.cu).
 namespace pb2 {
+// An NVTX range named after a C-ABI entry point around the call (host
+// side: argument checks, tensor-map encoding, launches), so a profiler
+// timeline shows which operator queued which kernels.  On only while the
+// environment variable PEARL_B200_NVTX is set (read once); NVTX v3 is
+// header-only and does nothing unless a profiler injects itself.
+bool nvtx_enabled();
+struct NvtxRange {
+  explicit NvtxRange(const char* name);
+  ~NvtxRange();
+  bool on;
+};
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
                  uint64_t inner, uint64_t outer, uint32_t box_inner, uint32_t box_outer,
                  CUtensorMapSwizzle swizzle);

@@ -4,7 +4,10 @@
 #include <atomic>
 #include <cstdio>
 #include <cstring>
+#include <cstdlib>
 #include <mutex>
+
+#include <nvtx3/nvToolsExt.h>
 
 #include "pb2_common.cuh"
 
@@ -112,6 +115,17 @@ __global__ void wait_selftest_kernel(SignalSync* sync, long long budget) {
 }
 
 int cuda_status(cudaError_t e) { return note_cuda(e); }
+
+bool nvtx_enabled() {
+  static const bool on = std::getenv("PEARL_B200_NVTX") != nullptr;
+  return on;
+}
+NvtxRange::NvtxRange(const char* name) : on(nvtx_enabled()) {
+  if (on) nvtxRangePushA(name);
+}
+NvtxRange::~NvtxRange() {
+  if (on) nvtxRangePop();
+}
 
 }  // namespace pb2
 

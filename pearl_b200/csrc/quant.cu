@@ -224,6 +224,7 @@ void launch_quant(const QuantArgs& a, cudaStream_t s) {
 }  // namespace pb2
 
 extern "C" int pb2_quantize(const pb2_quant_params* pp, void* stream) {
+  pb2::NvtxRange nvtx_range("pb2_quantize");
   using namespace pb2;
   if (!pp) return PB2_ERR_INVALID_ARGUMENT;
   const pb2_quant_params& p = *pp;
@@ -272,6 +273,7 @@ __global__ void rcp_approx_kernel(const float* in, float* out, int64_t n) {
 }  // namespace pb2
 
 extern "C" int pb2_rcp_approx_f32(int device, const float* in, float* out, int64_t n, void* stream) {
+  pb2::NvtxRange nvtx_range("pb2_rcp_approx_f32");
   using namespace pb2;
   if (n < 0 || (n > 0 && (!in || !out))) return PB2_ERR_INVALID_ARGUMENT;
   int st = set_device(device);

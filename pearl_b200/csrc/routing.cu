@@ -118,6 +118,7 @@ extern "C" int64_t pb2_build_routing_data_scratchpad_bytes(int64_t numel) {
 }
 
 extern "C" int pb2_build_routing_data(const pb2_routing_params* pp, void* stream) {
+  pb2::NvtxRange nvtx_range("pb2_build_routing_data");
   using namespace pb2;
   if (!pp) return PB2_ERR_INVALID_ARGUMENT;
   const pb2_routing_params& p = *pp;

@@ -28,6 +28,7 @@ __global__ void __launch_bounds__(kThreads) scatter_rows_kernel(const uint4* __r
 }  // namespace pb2
 
 extern "C" int pb2_scatter_rows(const pb2_scatter_params* pp, void* stream) {
+  pb2::NvtxRange nvtx_range("pb2_scatter_rows");
   using namespace pb2;
   if (!pp) return PB2_ERR_INVALID_ARGUMENT;
   const pb2_scatter_params& p = *pp;

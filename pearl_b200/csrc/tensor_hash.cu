@@ -373,6 +373,7 @@ extern "C" int64_t pb2_required_scratchpad_bytes(int64_t matrix_bytes, int threa
 }
 
 extern "C" int pb2_tensor_hash(const pb2_tensor_hash_params* pp, void* stream) {
+  pb2::NvtxRange nvtx_range("pb2_tensor_hash");
   using namespace pb2;
   if (!pp) return PB2_ERR_INVALID_ARGUMENT;
   const pb2_tensor_hash_params& p = *pp;
@@ -432,6 +433,7 @@ extern "C" int64_t pb2_merkle_nodes(int64_t len) {
 }
 
 extern "C" int pb2_merkle_layers(const pb2_merkle_params* pp, void* stream) {
+  pb2::NvtxRange nvtx_range("pb2_merkle_layers");
   using namespace pb2;
   if (!pp) return PB2_ERR_INVALID_ARGUMENT;
   const pb2_merkle_params& p = *pp;
@@ -466,6 +468,7 @@ extern "C" int pb2_merkle_layers(const pb2_merkle_params* pp, void* stream) {
 }
 
 extern "C" int pb2_commitment_hash_from_merkle_roots(const pb2_commitment_params* pp, void* stream) {
+  pb2::NvtxRange nvtx_range("pb2_commitment_hash_from_merkle_roots");
   using namespace pb2;
   if (!pp) return PB2_ERR_INVALID_ARGUMENT;
   const pb2_commitment_params& p = *pp;
