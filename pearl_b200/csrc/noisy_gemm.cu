@@ -265,6 +265,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int nden = kDenoise ? 4 : 0;  // 2 products x 2R bytes of fp16 K = 4 units of R bytes
   const int units = nmain + nden;
   constexpr int den_stages_per_product = 2 * kSPU;
+  // The producer asks L2 for the next round's first K stages when it reaches
+  // main unit pf_unit of the current round (a few units before the tile end).
+  constexpr int kPrefetchLead = 8;
+  const int pf_unit = nmain > kPrefetchLead ? nmain - kPrefetchLead : 0;
+  const int pf_stages = min(4, nmain * kSPU);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
@@ -345,6 +350,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         // loops are kept apart (and the tensor maps named, not selected), so
         // the per-stage code on the main path stays minimal.
         for (int u = 0; u < nmain && ok; ++u) {
+          if (u == pf_unit && leader && t0 + stride < a.num_tiles) {
+            // The next round's first K stages into L2, so its first units
+            // do not wait a full HBM round trip right after the tile end
+            // (where the ring has just held the denoise operands).
+            const int t1 = t0 + stride;
+            const bool two1 = a.tpr == 2 && t1 + 1 < a.num_tiles;
+            for (int s = 0; s < (two1 ? 2 : 1); ++s) {
+              const TileRef rn = tile_of(a, x, t1 + s);
+              const ExpertEntry& En = x.ex[rn.e];
+              const int mn = rn.tm * BM + int(rank) * BMC;
+              const int nn = En.b_row0 + rn.tn * kTN + int(rank) * (kTN / 2);
+              for (int st = 0; st < pf_stages; ++st) {
+                tma_prefetch_l2_2d(&En.tmA, st * BK, mn);
+                tma_prefetch_l2_2d(&a.tmB, st * BK, nn);
+              }
+            }
+          }
           for (int s = 0; s < (two ? 2 : 1) && ok; ++s) {
             const int m0 = s ? mb : ma, n0 = s ? nb : na;
             const CUtensorMap* tmA = s ? &Eb.tmA : &Ea.tmA;
@@ -483,9 +505,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // 32-column loads of a strip are in flight before the wait.
     //
     // Fold of one R-chunk u: each thread XORs its row's strip values into the
-    // four column classes (col / 2) % 4 of the hash tiles and pairs rows r and
-    // r + 8 with one shuffle (lanes with bit 3 clear keep classes 0 and 1,
-    // their partners 2 and 3).  Word w = u % 16 of a transcript is rotated
+    // four column classes (col / 2) % 4 of the hash tiles (rows r and r + 8
+    // meet in the transcript word's atomics).  Word w = u % 16 of a transcript is rotated
     // by 13 at each later chunk with the same w, so the final transcript is
     // the XOR over chunks of rotl(fold_u, 13 * (later chunks on w)); the
     // rotation is linear, so every strip warp pre-rotates its partial fold
@@ -497,13 +518,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int fw = warp - 2;
     const int q = warp & 3;
     const int wi = fw >> 2;
-    const bool is_low = (lane & 8) == 0;
     const uint32_t strip_off = (uint32_t(32 * q) << 16) + 64 * wi;
     // Slot releases go to the leader's acc_empty (remotely from the peer).
     const uint32_t rel_base = mapa(&S.acc_empty[0], 0);
-    // Transcript words this lane XORs into: row pair (lane % 8) + 8 (lane / 16),
-    // classes c0 and c0 + 1.
-    const int lane_tile = q * 64 + (is_low ? 0 : 2) * 16 + (lane & 7) + 8 * (lane >> 4);
+    // Transcript words this lane XORs into: row pair (lane % 8) + 8 (lane / 16)
+    // of lane quadrant q, class c at + 16 c.
+    const int lane_tile = q * 64 + (lane & 7) + 8 * (lane >> 4);
     uint32_t fpar = 0;  // acc_full parity per slot
     bool ok = true;
 
@@ -558,13 +578,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive_relaxed_cluster(rel_base + 8 * s);
         }
       };
-      // Pairs rows r and r + 8 and XORs the pre-rotated fold into the tile's
-      // transcript word.
+      // XORs the pre-rotated class folds into the tile's four transcript
+      // words (one per column class).  Rows r and r + 8 of a hash tile sit in
+      // lanes l and l ^ 8, which XOR into the same words: the atomics pair
+      // them, so no shuffle is needed (fewer instructions per event than a
+      // shuffle-and-select pairing, on sub-partitions the issuer and the
+      // producer share with these warps).
       auto commit_fold = [&](uint32_t p0, uint32_t p1, uint32_t p2, uint32_t p3) -> bool {
-        const uint32_t g0 = __shfl_xor_sync(0xffffffffu, is_low ? p2 : p0, 8);
-        const uint32_t g1 = __shfl_xor_sync(0xffffffffu, is_low ? p3 : p1, 8);
-        const uint32_t f0 = (is_low ? p0 : p2) ^ g0;
-        const uint32_t f1 = (is_low ? p1 : p3) ^ g1;
         const int w = u & 15;
         const int later = ((nmain - 1 - w) >> 4) - (u >> 4);  // chunks after u that hit word w
         const int rot = (13 * later) & 31;
@@ -574,8 +594,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             !(ok = mbar_wait_idle_warp(&S.xfree[b], ((round >> 1) - 1) & 1, abort_flag, a.sync, a.wait_budget)))
           return false;
         uint32_t* tw = xbuf + b * (16 * 256) + w * 256 + lane_tile;
-        atomicXor(tw, __funnelshift_l(f0, f0, rot));
-        atomicXor(tw + 16, __funnelshift_l(f1, f1, rot));
+        atomicXor(tw, __funnelshift_l(p0, p0, rot));
+        atomicXor(tw + 16, __funnelshift_l(p1, p1, rot));
+        atomicXor(tw + 32, __funnelshift_l(p2, p2, rot));
+        atomicXor(tw + 48, __funnelshift_l(p3, p3, rot));
         // The reference counts one hash per 2 x 64 tile of each 128-row
         // tile that starts inside M.
         if (kDebug && lane == 0 && tm * BM + int(rank) * BMC < E.m) atomicAdd(a.counter, 16ull);
@@ -595,70 +617,106 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
 
+      // The 16 words of class c in a 64-column strip (columns 8j + 2c and
+      // 8j + 2c + 1 of both halves) as a depth-3 tree of 3-input XORs.
+      auto class_fold = [](const uint32_t* a, const uint32_t* b, int c) -> uint32_t {
+        const uint32_t t0 = a[2 * c] ^ a[2 * c + 1] ^ a[8 + 2 * c];
+        const uint32_t t1 = a[9 + 2 * c] ^ a[16 + 2 * c] ^ a[17 + 2 * c];
+        const uint32_t t2 = a[24 + 2 * c] ^ a[25 + 2 * c] ^ b[2 * c];
+        const uint32_t t3 = b[2 * c + 1] ^ b[8 + 2 * c] ^ b[9 + 2 * c];
+        const uint32_t t4 = b[16 + 2 * c] ^ b[17 + 2 * c] ^ b[24 + 2 * c];
+        return (t0 ^ t1 ^ t2) ^ (t3 ^ t4 ^ b[25 + 2 * c]);
+      };
+
       if (!do_convert && !do_store) {
         // ---- every chunk but a tile's last: fold only
-        uint32_t p0 = 0, p1 = 0, p2 = 0, p3 = 0;
         uint32_t v0[32], v1[32];
         __syncwarp();
         tmem_ld32(taddr, v0);  // both halves in flight, one wait
         tmem_ld32(taddr + 32, v1);
-        tmem_wait_ld_into(v0);
-        tmem_wait_ld_into(v1);
+        tmem_wait_ld_into2(v0, v1);
         release(false);
-        fold32(v0, p0, p1, p2, p3);
-        fold32(v1, p0, p1, p2, p3);
-        commit_fold(p0, p1, p2, p3);
+        commit_fold(class_fold(v0, v1, 0), class_fold(v0, v1, 1), class_fold(v0, v1, 2), class_fold(v0, v1, 3));
         return;
       }
       // ---- a tile's last chunk (fold + f32 rewrite, or fold + C) or its final C.
-      // C goes out half by half before the release, so no more than one
-      // 32-column half is live (a spill-free kernel at 96 registers); the
-      // release comes one box store later than it could, once per slot and
-      // tile.
+      // Both paths give the slot back as soon as its TMEM has been read (or
+      // rewritten): the issuer waits for that release before the denoise
+      // MMAs or the slot's next tile, and both slots reach their tile ends
+      // together, so the tensor pipe idles for as long as this takes.
+      uint32_t p0 = 0, p1 = 0, p2 = 0, p3 = 0;
+      // With 128-wide tiles the strips beyond the tile hold nothing to store.
+      const bool strip_live = 64 * wi < kTN;
+      if (do_convert) {
+        // Both halves in flight (as in the fold-only path), one load wait,
+        // one store wait: S as f32 * 2^-12 for the f16 denoise MMAs (folded
+        // first).
+        if (strip_live) {
+          uint32_t v0[32], v1[32];
+          __syncwarp();
+          tmem_ld32(taddr, v0);
+          tmem_ld32(taddr + 32, v1);
+          tmem_wait_ld_into(v0);
+          tmem_wait_ld_into(v1);
+          if (do_fold) {
+            fold32(v0, p0, p1, p2, p3);
+            fold32(v1, p0, p1, p2, p3);
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v0[i] = __float_as_uint(float(int(v0[i])) * (1.0f / 4096.0f));
+          tmem_st32(taddr, v0);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v1[i] = __float_as_uint(float(int(v1[i])) * (1.0f / 4096.0f));
+          tmem_st32(taddr + 32, v1);
+          tmem_wait_st();
+        }
+        release(true);
+        if (do_fold) commit_fold(p0, p1, p2, p3);
+        return;
+      }
+      // C: the halves are read one at a time (one 32-column half live: a
+      // spill-free kernel at 96 registers).  The first half goes into the
+      // warp's shared-memory box and out by TMA before the second is read;
+      // the slot is released right after the second read, so the second
+      // box write -- which waits for the first TMA store to have read the
+      // box -- is off the release path.
       float rs = 0.f;
       float2 sbv = make_float2(0.f, 0.f);
-      if (do_store) {  // scales first: their latency overlaps the loads
+      {  // scales first: their latency overlaps the loads
         const int row = tm * BM + int(rank) * BMC + 32 * q + lane;
         rs = (row < E.m ? E.sA[a.scale_per_tensor ? 0 : row] : 0.0f) * (is_main ? 1.0f : 4096.0f);
         const int c = tn * kTN + 64 * wi + 2 * lane;  // this lane's two column scales
         if (c < a.N)
           sbv = a.scale_per_tensor ? make_float2(E.sB[0], E.sB[0]) : *reinterpret_cast<const float2*>(E.sB + c);
       }
-      const int row0 = tm * BM + int(rank) * BMC + 32 * q;
-      uint8_t* box = cstage + fw * kCBoxBytes;
-      uint32_t p0 = 0, p1 = 0, p2 = 0, p3 = 0;
-      // With 128-wide tiles the strips beyond the tile hold nothing to store.
-      const bool strip_live = 64 * wi < kTN;
+      auto pack_half = [&](const uint32_t* v, int h, uint32_t* packed) {
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        if (!strip_live) break;
-        uint32_t v[32];
-        __syncwarp();
-        tmem_ld32(taddr + 32 * h, v);
-        tmem_wait_ld_into(v);
-        if (do_fold) fold32(v, p0, p1, p2, p3);
-        if (do_convert) {
-          // S as f32 * 2^-12 for the f16 denoise MMAs (folded above first).
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(float(int(v[i])) * (1.0f / 4096.0f));
-          tmem_st32(taddr + 32 * h, v);
+        for (int i = 0; i < 32; i += 2) {
+          const int src = 16 * h + i / 2;  // lane holding columns 32h + i, +1
+          const float bx = __shfl_sync(0xffffffffu, sbv.x, src);
+          const float by = __shfl_sync(0xffffffffu, sbv.y, src);
+          const float f0 = (is_main && kKind == 0) ? float(int(v[i])) : __uint_as_float(v[i]);
+          const float f1 = (is_main && kKind == 0) ? float(int(v[i + 1])) : __uint_as_float(v[i + 1]);
+          packed[i / 2] = pack_bf16(f0 * rs * bx, f1 * rs * by);
         }
-        if (do_store) {
-          uint32_t packed[16];
+      };
+      if (strip_live) {
+        const int row0 = tm * BM + int(rank) * BMC + 32 * q;
+        uint8_t* box = cstage + fw * kCBoxBytes;
 #pragma unroll
-          for (int i = 0; i < 32; i += 2) {
-            const int src = 16 * h + i / 2;  // lane holding columns 32h + i, +1
-            const float bx = __shfl_sync(0xffffffffu, sbv.x, src);
-            const float by = __shfl_sync(0xffffffffu, sbv.y, src);
-            const float f0 = (is_main && kKind == 0) ? float(int(v[i])) : __uint_as_float(v[i]);
-            const float f1 = (is_main && kKind == 0) ? float(int(v[i + 1])) : __uint_as_float(v[i + 1]);
-            packed[i / 2] = pack_bf16(f0 * rs * bx, f1 * rs * by);
-          }
-          store_c_packed(&E.tmC, box, packed, row0, tn * kTN + 64 * wi + 32 * h, lane);
+        for (int h = 0; h < 2; ++h) {
+          uint32_t v[32], pk[16];
+          __syncwarp();
+          tmem_ld32(taddr + 32 * h, v);
+          tmem_wait_ld_into(v);
+          if (do_fold) fold32(v, p0, p1, p2, p3);
+          if (h == 1) release(false);
+          pack_half(v, h, pk);
+          store_c_packed(&E.tmC, box, pk, row0, tn * kTN + 64 * wi + 32 * h, lane);
         }
+      } else {
+        release(false);
       }
-      if (do_convert) tmem_wait_st();
-      release(do_convert);
       if (do_fold) commit_fold(p0, p1, p2, p3);
     };
 

@@ -527,6 +527,14 @@ __host__ __device__ constexpr uint32_t idesc_f8(int m, int n, uint32_t afmt, uin
 
 // 2-D tiled load into this CTA's shared memory whose transaction bytes are
 // counted on the leader CTA's barrier at the same offset.
+// Bring one box of a 2-D tensor map into L2 (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d_2sm(const CUtensorMap* map, uint64_t* bar, void* dst,
                                                 int x, int y) {
   const uint32_t leader_bar = smem_u32(bar) & 0xFEFFFFFFu;
@@ -604,6 +612,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* v) {
 __device__ __forceinline__ void tmem_wait_ld_into(uint32_t* v) {
   asm volatile("tcgen05.wait::ld.sync.aligned;"
                : PB2_T8(v, 0), PB2_T8(v, 8), PB2_T8(v, 16), PB2_T8(v, 24)
+               :
+               : "memory");
+}
+// One tcgen05.wait::ld for two 32-register loads in flight.
+__device__ __forceinline__ void tmem_wait_ld_into2(uint32_t* a, uint32_t* b) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : PB2_T8(a, 0), PB2_T8(a, 8), PB2_T8(a, 16), PB2_T8(a, 24), PB2_T8(b, 0), PB2_T8(b, 8),
+                 PB2_T8(b, 16), PB2_T8(b, 24)
                :
                : "memory");
 }
