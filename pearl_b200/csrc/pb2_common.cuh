@@ -525,8 +525,6 @@ __host__ __device__ constexpr uint32_t idesc_f8(int m, int n, uint32_t afmt, uin
   return (1u << 4) | (afmt << 7) | (bfmt << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
 }
 
-// 2-D tiled load into this CTA's shared memory whose transaction bytes are
-// counted on the leader CTA's barrier at the same offset.
 // Bring one box of a 2-D tensor map into L2 (no shared memory, no barrier).
 __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
   asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
@@ -535,6 +533,8 @@ __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x
                : "memory");
 }
 
+// 2-D tiled load into this CTA's shared memory whose transaction bytes are
+// counted on the leader CTA's barrier at the same offset.
 __device__ __forceinline__ void tma_load_2d_2sm(const CUtensorMap* map, uint64_t* bar, void* dst,
                                                 int x, int y) {
   const uint32_t leader_bar = smem_u32(bar) & 0xFEFFFFFFu;
