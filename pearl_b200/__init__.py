@@ -42,6 +42,8 @@ from . import moe
 from . import quantization
 from . import device_waits
 from . import fp8
+from . import merkle
+from . import proof
 from . import ops  # noqa: F401  (registers torch.ops.pearl_gemm.*)
 
 __all__ = [
