@@ -109,3 +109,88 @@ def test_reference_wrappers_reach_the_interface_with_every_argument_in_place():
         print("ok", len(real))
     """)
     assert out.strip() == "ok 9"
+
+
+# The reference's vLLM plugin package (miner/vllm-miner) on this library.  Its
+# imports reach two modules that are not Python in the reference: the Rust
+# extension pearl_mining and the third-party bitcoinutils (gateway address
+# helpers).  Only those are stubbed, inside the child interpreter.
+_STUB_HOOK = """
+import importlib.abc, importlib.machinery, sys, types
+class _Stub(types.ModuleType):
+    def __getattr__(self, n):
+        if n.startswith("__"):
+            raise AttributeError(n)
+        if n.isupper():
+            return 64  # size constants used at import time
+        return type(n, (), {"__init__": lambda self, *a, **k: None})
+class _Finder(importlib.abc.MetaPathFinder, importlib.abc.Loader):
+    def find_spec(self, name, path, target=None):
+        if name.split(".")[0] in ("pearl_mining", "bitcoinutils"):
+            return importlib.machinery.ModuleSpec(name, self, is_package=True)
+        return None
+    def create_module(self, spec):
+        return _Stub(spec.name)
+    def exec_module(self, m):
+        m.__path__ = []
+sys.meta_path.insert(0, _Finder())
+"""
+
+
+def _run_miner(code: str) -> str:
+    src = _reference_src()
+    if src is None:
+        pytest.skip("no reference checkout (set PEARL_REFERENCE)")
+    miner = os.path.dirname(os.path.dirname(src))
+    paths = [os.path.join(ROOT, "pearl_b200", "compat"), ROOT, src] + [
+        os.path.join(miner, p, "src") for p in ("miner-base", "miner-utils", "pearl-gateway", "vllm-miner")]
+    env = dict(os.environ)
+    env["PYTHONPATH"] = os.pathsep.join(paths)
+    res = subprocess.run([sys.executable, "-c", _STUB_HOOK + textwrap.dedent(code)], env=env, capture_output=True,
+                         text=True, timeout=600, cwd=ROOT)
+    assert res.returncode == 0, res.stdout + res.stderr
+    return res.stdout
+
+
+def test_reference_vllm_plugin_registers_on_the_shim():
+    """vllm_miner.register.register_pearl_miner_layer (register.py:32-50)
+    registers the reference's "pearl" quantization config with vLLM while
+    pearl_gemm_cuda is this library's shim."""
+    out = _run_miner("""
+        import pearl_gemm_cuda
+        import pearl_b200.pearl_gemm_cuda as shim
+        from vllm_miner.register import register_pearl_miner_layer
+        register_pearl_miner_layer()
+        from vllm.model_executor.layers.quantization import QUANTIZATION_METHODS, get_quantization_config
+        from vllm_miner.vllm_config import PearlConfig
+        assert pearl_gemm_cuda is shim
+        assert "pearl" in QUANTIZATION_METHODS and get_quantization_config("pearl") is PearlConfig
+        print("ok")
+    """)
+    assert out.strip().endswith("ok")
+
+
+def test_reference_vanilla_operator_reaches_the_interface():
+    """vllm_miner.gemm_operators.pearl_gemm_vanilla (gemm_operators.py:28-65),
+    the non-mining branch of PearlScheme.apply_weights, calls pearl_gemm.gemm
+    with its operands, scales and the output it allocates; on the shim that
+    call lands in pearl_b200.pearl_gemm_interface.gemm (replaced by a
+    recorder: nothing is launched on the CPU)."""
+    out = _run_miner("""
+        import torch
+        import pearl_b200.pearl_gemm_interface as I
+        calls = []
+        I.gemm = lambda *a, **k: calls.append((a, k))
+        import vllm_miner.gemm_operators as G
+        A = torch.zeros(4, 64, dtype=torch.int8)
+        B = torch.zeros(8, 64, dtype=torch.int8)
+        sa, sb = torch.ones(4), torch.ones(8)
+        C = G.pearl_gemm_vanilla(A, B, sa, sb, torch.bfloat16)
+        assert len(calls) == 1
+        args, kw = calls[0]
+        assert args[0] is A and args[1] is B and args[2] is sa and args[3] is sb and args[4] is C
+        assert C.shape == (4, 8) and C.dtype == torch.bfloat16
+        assert (kw["tile_size_m"], kw["tile_size_n"], kw["tile_size_k"]) == (128, 256, 128)
+        print("ok")
+    """)
+    assert out.strip().endswith("ok")
