@@ -52,10 +52,13 @@ def test_tensor_hash_matches_oracle(rows, cols):
     assert _gpu_tensor_hash(data.cuda(), key) == want
 
 
-@pytest.mark.parametrize("tpb", [256, 512])
-def test_tensor_hash_group_sizes(tpb):
-    g = torch.Generator().manual_seed(tpb)
-    data = torch.randint(-128, 128, (777, 3000), generator=g, dtype=torch.int8)
+# Ragged tails, exactly one group (the root applied inside the group), and
+# whole groups only (every group on the staged-copy path).
+@pytest.mark.parametrize("tpb,rows,cols", [(256, 777, 3000), (512, 777, 3000), (256, 256, 1024),
+                                           (512, 512, 1024), (512, 1024, 2048), (256, 300, 1024)])
+def test_tensor_hash_group_sizes(tpb, rows, cols):
+    g = torch.Generator().manual_seed(tpb + rows)
+    data = torch.randint(-128, 128, (rows, cols), generator=g, dtype=torch.int8)
     key = bytes(range(32))
     want = O.tensor_hash(data.numpy(), key)
     assert _gpu_tensor_hash(data.cuda().view(torch.uint8), key, tpb) == want
