@@ -116,6 +116,8 @@ __device__ __forceinline__ void load_vec(const QuantArgs& a, int row, int vec, b
 template <typename T>
 __global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const QuantArgs a) {
   __shared__ float warp_max[kQuantThreads / 32];
+  griddep_wait();  // launched early behind the previous kernel (programmatic dependent launch)
+  griddep_launch_dependents();
   const int row = blockIdx.x;
   const int nvec = a.n / 8;
   const int iters = (nvec + kQuantThreads - 1) / kQuantThreads;
@@ -160,6 +162,8 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const QuantAr
 template <typename T, int kIters, int kThreads>
 __global__ void __launch_bounds__(kThreads, 1024 / kThreads) quant_rows_reg_kernel(const QuantArgs a) {
   __shared__ float warp_max[kThreads / 32];
+  griddep_wait();  // launched early behind the previous kernel (programmatic dependent launch)
+  griddep_launch_dependents();
   const int row = blockIdx.x;
   const int nvec = a.n / 8;
   uint4 raw[kIters];
@@ -203,21 +207,38 @@ __global__ void __launch_bounds__(kThreads, 1024 / kThreads) quant_rows_reg_kern
   }
 }
 
+// Launched with programmatic stream serialization: the grid is scheduled
+// while the previous kernel drains and waits for it in griddep_wait, and it
+// lets the next kernel (the GEMM reading its output) start its own set-up.
+template <typename K>
+void launch_pdl(K kernel, int blocks, int threads, const QuantArgs& a, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(blocks), 1, 1);
+  cfg.blockDim = dim3(unsigned(threads), 1, 1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, a);
+}
+
 template <typename T>
 void launch_quant(const QuantArgs& a, cudaStream_t s) {
   // Four 16-byte vectors per thread and 1024 resident threads per SM: 64 KB
   // of each SM's loads in flight whatever the row length.
   const int nvec = a.n / 8;
   if (nvec <= 256)
-    quant_rows_reg_kernel<T, 4, 64><<<a.m, 64, 0, s>>>(a);
+    launch_pdl(quant_rows_reg_kernel<T, 4, 64>, a.m, 64, a, s);
   else if (nvec <= 512)
-    quant_rows_reg_kernel<T, 4, 128><<<a.m, 128, 0, s>>>(a);
+    launch_pdl(quant_rows_reg_kernel<T, 4, 128>, a.m, 128, a, s);
   else if (nvec <= 1024)
-    quant_rows_reg_kernel<T, 4, 256><<<a.m, 256, 0, s>>>(a);
+    launch_pdl(quant_rows_reg_kernel<T, 4, 256>, a.m, 256, a, s);
   else if (nvec <= 2048)
-    quant_rows_reg_kernel<T, 4, 512><<<a.m, 512, 0, s>>>(a);
+    launch_pdl(quant_rows_reg_kernel<T, 4, 512>, a.m, 512, a, s);
   else
-    quant_rows_kernel<T><<<a.m, kQuantThreads, 0, s>>>(a);
+    launch_pdl(quant_rows_kernel<T>, a.m, kQuantThreads, a, s);
 }
 
 }  // namespace
