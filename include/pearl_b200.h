@@ -367,11 +367,24 @@ typedef struct pb2_gemm_params {
   int64_t hit_capacity;
   uint32_t* transcripts; /* (m/2)*(n/64) * 16 words */
   uint32_t* digests;     /* (m/2)*(n/64) * 8 words  */
+  /* pb2_gemm only (optional): scratch for a K split of a GEMM with too few
+   * tiles to fill the SMs (a decode batch), pb2_gemm_workspace_bytes() bytes,
+   * 16-byte aligned, on `device`.  Null or smaller: no split. */
+  int32_t* workspace;
+  int64_t workspace_bytes;
 } pb2_gemm_params;
 PB2_API int pb2_noisy_gemm(const pb2_gemm_params* p, void* stream);
 /* Plain scaled GEMM: C = bf16(A_scales * (A . B^T) * B_scales), reading the
- * operands from p->ApEA / p->BpEB (the reference passes A and B there). */
+ * operands from p->ApEA / p->BpEB (the reference passes A and B there).
+ * No reference counterpart for the workspace: when few 256 x 256 tiles
+ * cover C (m a decode batch), K is cut into equal ranges, every (tile, range)
+ * runs on its own SM pair and writes its exact int32 partial to the
+ * workspace, and a second kernel sums the ranges and applies the scales --
+ * the same C, bit for bit, as without the split. */
 PB2_API int pb2_gemm(const pb2_gemm_params* p, void* stream);
+/* Bytes of workspace pb2_gemm would use for this shape on `device` (0: it
+ * would not split K). */
+PB2_API int64_t pb2_gemm_workspace_bytes(int device, int64_t m, int64_t n, int64_t k);
 
 /* ------------------------------------------------------ FP8 mined GEMM ---
  * No reference counterpart: the protocol defines mined GEMMs of 7-bit

@@ -31,7 +31,7 @@ EXPORTED = [
     "pb2_host_signal_header_size", "pb2_host_signal_sync_size", "pb2_status_string",
     "pb2_last_cuda_error", "pb2_abi_version", "pb2_noise_gen", "pb2_noise_A", "pb2_noise_B", "pb2_noise_AB",
     "pb2_denoise_converter", "pb2_noisy_gemm", "pb2_gemm", "pb2_inner_hash",
-    "pb2_noisy_gemm_static_scratch", "pb2_tensor_hash", "pb2_required_scratchpad_bytes",
+    "pb2_noisy_gemm_static_scratch", "pb2_tensor_hash", "pb2_required_scratchpad_bytes", "pb2_gemm_workspace_bytes",
     "pb2_commitment_hash_from_merkle_roots", "pb2_build_routing_data",
     "pb2_build_routing_data_scratchpad_bytes", "pb2_quantize", "pb2_scatter_rows",
     "pb2_merkle_layers", "pb2_merkle_nodes", "pb2_set_wait_budget_cycles", "pb2_wait_selftest",
@@ -80,7 +80,8 @@ class GemmParams(ctypes.Structure):
                 ("k_blocks_per_split_noising_b", ctypes.c_int),
                 ("skip_reduction", ctypes.c_int), ("skip_denoising", ctypes.c_int),
                 ("inner_hash_counter", _vp), ("enable_debug", ctypes.c_int),
-                ("hits", _vp), ("hit_capacity", _i64), ("transcripts", _vp), ("digests", _vp)]
+                ("hits", _vp), ("hit_capacity", _i64), ("transcripts", _vp), ("digests", _vp),
+                ("workspace", _vp), ("workspace_bytes", _i64)]
 
 
 class Fp8GemmParams(ctypes.Structure):
@@ -168,6 +169,8 @@ def load() -> ctypes.CDLL:
         L.pb2_merkle_nodes.argtypes = [_i64]
         L.pb2_required_scratchpad_bytes.restype = _i64
         L.pb2_required_scratchpad_bytes.argtypes = [_i64, ctypes.c_int]
+        L.pb2_gemm_workspace_bytes.restype = _i64
+        L.pb2_gemm_workspace_bytes.argtypes = [ctypes.c_int, _i64, _i64, _i64]
         L.pb2_host_signal_header_size.restype = _i64
         L.pb2_host_signal_sync_size.restype = _i64
         L.pb2_status_string.restype = ctypes.c_char_p

@@ -66,6 +66,11 @@ struct MainArgs {
   int tiles_n, num_tiles, group;
   int tpr;  // tiles a CTA pair runs per round: 2 (two TMEM slots in alternation) or 1
   int scale_per_tensor;  // sA[0] and sB[0] scale every row and column (FP8 operands)
+  // Plain GEMM only: K split into `ksplit` equal ranges, one work item per
+  // (tile, range); each item writes its exact int32 partial to ws[range] and
+  // a reduction kernel sums the ranges and scales (1: no split).
+  int ksplit;
+  int32_t* ws;  // (ksplit, m, N) int32
   SignalSync* sync;  // where a timed-out wait records its error
   const uint32_t* target;
   const uint32_t* key;
@@ -104,6 +109,7 @@ struct ExpertTable {
 
 struct TileRef {
   int e, tm, tn;
+  int ks;  // K range of a split-K work item (0 without a split)
 };
 
 struct Smem {
@@ -135,7 +141,18 @@ __device__ __forceinline__ TileRef tile_of(const MainArgs& a, const ExpertTable<
   const int first_m = g * group;
   const int gm = min(group, E.tiles_m - first_m);
   const int within = lt - g * gsize;
-  return TileRef{e, first_m + within % gm, within / gm};
+  return TileRef{e, first_m + within % gm, within / gm, 0};
+}
+
+// Work item t of the launch: tile t, or with a K split tile t / ksplit and
+// K range t % ksplit (the ranges of one tile follow one another).
+template <int kE>
+__device__ __forceinline__ TileRef item_of(const MainArgs& a, const ExpertTable<kE>& x, int t) {
+  if (a.ksplit <= 1) return tile_of(a, x, t);
+  const int tile = t / a.ksplit;
+  TileRef r = tile_of(a, x, tile);
+  r.ks = t - tile * a.ksplit;
+  return r;
 }
 
 // Per-slot phase bits packed in one word (bit s = parity of slot s).
@@ -261,7 +278,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // transcript and denoise the chunk length only sets the interleaving.
   constexpr int unit_k = kSPU * BK;  // = R with transcript or denoise (host-checked)
   constexpr int stages_per_unit = kSPU;
-  const int nmain = a.K / unit_k;
+  const int ksplit = a.ksplit > 1 ? a.ksplit : 1;
+  const int nmain = a.K / unit_k / ksplit;  // units of one work item
   constexpr int nden = kDenoise ? 4 : 0;  // 2 products x 2R bytes of fp16 K = 4 units of R bytes
   const int units = nmain + nden;
   constexpr int den_stages_per_product = 2 * kSPU;
@@ -339,8 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int t0 = first; t0 < a.num_tiles && ok; t0 += stride) {
         const bool two = a.tpr == 2 && t0 + 1 < a.num_tiles;
-        const TileRef r0 = tile_of(a, x, t0);
-        const TileRef r1 = two ? tile_of(a, x, t0 + 1) : r0;
+        const TileRef r0 = item_of(a, x, t0);
+        const TileRef r1 = two ? item_of(a, x, t0 + 1) : r0;
         const ExpertEntry& Ea = x.ex[r0.e];
         const ExpertEntry& Eb = x.ex[r1.e];
         // This CTA's 128 rows of A (of its problem) and half of the B rows, per slot.
@@ -357,24 +375,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int t1 = t0 + stride;
             const bool two1 = a.tpr == 2 && t1 + 1 < a.num_tiles;
             for (int s = 0; s < (two1 ? 2 : 1); ++s) {
-              const TileRef rn = tile_of(a, x, t1 + s);
+              const TileRef rn = item_of(a, x, t1 + s);
               const ExpertEntry& En = x.ex[rn.e];
               const int mn = rn.tm * BM + int(rank) * BMC;
               const int nn = En.b_row0 + rn.tn * kTN + int(rank) * (kTN / 2);
               for (int st = 0; st < pf_stages; ++st) {
-                tma_prefetch_l2_2d(&En.tmA, st * BK, mn);
-                tma_prefetch_l2_2d(&a.tmB, st * BK, nn);
+                const int kx = rn.ks * nmain * unit_k + st * BK;
+                tma_prefetch_l2_2d(&En.tmA, kx, mn);
+                tma_prefetch_l2_2d(&a.tmB, kx, nn);
               }
             }
           }
           for (int s = 0; s < (two ? 2 : 1) && ok; ++s) {
             const int m0 = s ? mb : ma, n0 = s ? nb : na;
+            const int kbase = (s ? r1.ks : r0.ks) * nmain;  // the item's K range (split-K), in units
             const CUtensorMap* tmA = s ? &Eb.tmA : &Ea.tmA;
             for (int st = 0; st < stages_per_unit; ++st, ++it) {
               const int j = it % kStages;
               if (!(ok = mbar_wait_warp(&S.empty[j], ((it / kStages) & 1) ^ 1, abort_flag, a.sync, a.wait_budget))) break;
               uint8_t* sa = stage_mem + j * kStageBytes;
-              const int kbyte = u * unit_k + st * BK;
+              const int kbyte = (kbase + u) * unit_k + st * BK;
               if (leader) {
                 // The leader CTA's full barrier counts both CTAs' bytes.
                 if (rank == 0) mbar_arrive_expect_tx(&S.full[j], 2 * kStageBytes);
@@ -700,7 +720,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           packed[i / 2] = pack_bf16(f0 * rs * bx, f1 * rs * by);
         }
       };
-      if (strip_live) {
+      if (strip_live && !kReduce && !kDenoise && a.ksplit > 1) {
+        // A split-K item: this lane's row of the exact int32 partial goes to
+        // ws[ks] as it is (whole 16-byte vectors: N % 8 == 0); the reduction
+        // kernel sums the ranges and scales.
+        const int row = tm * BM + int(rank) * BMC + 32 * q + lane;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t v[32];
+          __syncwarp();
+          tmem_ld32(taddr + 32 * h, v);
+          tmem_wait_ld_into(v);
+          if (h == 1) release(false);
+          const int col = tn * kTN + 64 * wi + 32 * h;
+          if (row < E.m) {
+            int32_t* dst = a.ws + (int64_t(tr.ks) * E.m + row) * int64_t(a.N) + col;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              if (col + 4 * j < a.N)
+                *reinterpret_cast<uint4*>(dst + 4 * j) = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          }
+        }
+      } else if (strip_live) {
         const int row0 = tm * BM + int(rank) * BMC + 32 * q;
         uint8_t* box = cstage + fw * kCBoxBytes;
 #pragma unroll
@@ -723,8 +764,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t it = 0;  // operand stages issued so far, in the issuer's order
     for (int t0 = first; t0 < a.num_tiles && ok; t0 += stride) {
       const bool two = a.tpr == 2 && t0 + 1 < a.num_tiles;
-      const TileRef r0 = tile_of(a, x, t0);
-      const TileRef r1 = two ? tile_of(a, x, t0 + 1) : r0;
+      const TileRef r0 = item_of(a, x, t0);
+      const TileRef r1 = two ? item_of(a, x, t0 + 1) : r0;
       const int round = (t0 - first) / stride;
       for (int u = 0; u < units && ok; ++u) {
         const bool is_main = u < nmain;
@@ -784,8 +825,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t0 = first; t0 < a.num_tiles && ok; t0 += stride) {
       const bool two = a.tpr == 2 && t0 + 1 < a.num_tiles;
       const int round = (t0 - first) / stride;
-      const TileRef r0 = tile_of(a, x, t0);
-      const TileRef r1 = two ? tile_of(a, x, t0 + 1) : r0;
+      const TileRef r0 = item_of(a, x, t0);
+      const TileRef r1 = two ? item_of(a, x, t0 + 1) : r0;
       hash_buffer(I0{}, round, r0);
       if (two && ok) hash_buffer(I1{}, round, r1);
     }
@@ -917,6 +958,69 @@ int make_shared_args(MainArgs& a, const pb2_gemm_params& p, int bk, int tn_width
   return PB2_OK;
 }
 
+// The K split of a plain GEMM whose 256 x 256 tiles are too few to fill the
+// SM pairs (a decode batch): the largest d <= 4 that divides K's 128-byte
+// units into ranges of at least kMinSplitUnits units and keeps tiles x d work
+// items within one round of pairs.  1: no split.  A split costs a write and
+// a read of d int32 partials of C and a second launch (measured ~8 us at
+// m = 256, n = 4096), so only long K ranges (the down projection's 14336)
+// gain from it.
+constexpr int64_t kMinSplitUnits = 24;
+int splitk_plan(int device, int64_t m, int64_t n, int64_t k) {
+  const int64_t tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
+  const int pairs = resident_pairs(device) ? resident_pairs(device) : std::max(1, sm_count(device) / 2);
+  const int64_t units = k / kTileK;
+  if (tiles >= pairs || k % kTileK != 0) return 1;
+  int best = 1;
+  for (int d = 2; d <= 4; ++d)
+    if (units % d == 0 && units / d >= kMinSplitUnits && tiles * d <= pairs) best = d;
+  return best;
+}
+
+// C = bf16(float(sum over the K ranges of the int32 partials) * sA * sB), the
+// epilogue's arithmetic in its order; one thread per 8 columns.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const int32_t* ws, int ksplit, int64_t m, int64_t n,
+                                                            const float* sA, const float* sB, int per_tensor,
+                                                            __nv_bfloat16* C) {
+  griddep_wait();  // launched behind the GEMM (programmatic dependent launch)
+  griddep_launch_dependents();
+  const int64_t vecs = n / 8;
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= m * vecs) return;
+  const int64_t row = i / vecs, col = (i - row * vecs) * 8;
+  int acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  for (int s = 0; s < ksplit; ++s) {
+    const int4* p = reinterpret_cast<const int4*>(ws + (int64_t(s) * m + row) * n + col);
+    const int4 x = p[0], y = p[1];
+    acc[0] += x.x; acc[1] += x.y; acc[2] += x.z; acc[3] += x.w;
+    acc[4] += y.x; acc[5] += y.y; acc[6] += y.z; acc[7] += y.w;
+  }
+  const float ra = sA[per_tensor ? 0 : row];
+  uint32_t out[4];
+#pragma unroll
+  for (int j = 0; j < 8; j += 2) {
+    const float b0 = sB[per_tensor ? 0 : col + j], b1 = sB[per_tensor ? 0 : col + j + 1];
+    out[j / 2] = pack_bf16(float(acc[j]) * ra * b0, float(acc[j + 1]) * ra * b1);
+  }
+  *reinterpret_cast<uint4*>(C + row * n + col) = make_uint4(out[0], out[1], out[2], out[3]);
+}
+
+int launch_splitk_reduce(const int32_t* ws, int ksplit, int64_t m, int64_t n, const float* sA, const float* sB,
+                         void* C, cudaStream_t s) {
+  const int64_t threads = m * (n / 8);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned((threads + 255) / 256), 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, splitk_reduce_kernel, ws, ksplit, m, n, sA, sB, 0, static_cast<__nv_bfloat16*>(C));
+  return launch_status();
+}
+
 }  // namespace
 
 // Every check of the main kernel's arguments that needs no CUDA call.
@@ -960,7 +1064,14 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
   // while they do not fill the pairs: more SMs streaming the weights.
   const int64_t tiles_m = (p.m + BM - 1) / BM;
   const int pairs_est = resident_pairs(p.device) ? resident_pairs(p.device) : std::max(1, sm_count(p.device) / 2);
-  const bool narrow = !reduce && !denoise && tiles_m * ((p.n + BN - 1) / BN) < 2 * int64_t(pairs_est);
+  // A plain GEMM with too few 256 x 256 tiles splits K when the caller gave
+  // the workspace; otherwise small problems take 128-wide tiles.
+  int ksplit = 1;
+  if (!reduce && !denoise && p.workspace) {
+    ksplit = splitk_plan(p.device, p.m, p.n, p.k);
+    if (ksplit > 1 && (p.workspace_bytes < int64_t(ksplit) * p.m * p.n * 4 || !al16(p.workspace))) ksplit = 1;
+  }
+  const bool narrow = ksplit == 1 && !reduce && !denoise && tiles_m * ((p.n + BN - 1) / BN) < 2 * int64_t(pairs_est);
   const int tn_width = narrow ? BN / 2 : BN;
   MainArgs a;
   std::memset(&a, 0, sizeof(a));
@@ -982,8 +1093,10 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
   e.hit_cap = p.hits ? p.hit_capacity : 0;
   e.transcripts = p.transcripts;
   e.digests = p.digests;
-  a.num_tiles = e.tiles_m * a.tiles_n;
-  a.tpr = (narrow && a.num_tiles <= pairs_est) ? 1 : 2;
+  a.num_tiles = e.tiles_m * a.tiles_n * ksplit;  // work items
+  a.tpr = ((narrow || ksplit > 1) && a.num_tiles <= pairs_est) ? 1 : 2;
+  a.ksplit = ksplit;
+  a.ws = ksplit > 1 ? p.workspace : nullptr;
   a.sync = e.sync;
 
   // Operand stages per unit: a unit is R bytes of K with transcript or
@@ -991,8 +1104,10 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
   // one 128-byte tile_size_k.
   const int spu = (reduce || denoise) ? int(p.r) / bk : kTileK / bk;
   if (bk == 64) return launch_spu<64, 1>(a, x, p.device, reduce, denoise, debug, false, s);
-  return spu == 2 ? launch_spu<128, 2>(a, x, p.device, reduce, denoise, debug, false, s)
-                  : launch_spu<128, 1>(a, x, p.device, reduce, denoise, debug, narrow, s);
+  st = spu == 2 ? launch_spu<128, 2>(a, x, p.device, reduce, denoise, debug, false, s)
+                : launch_spu<128, 1>(a, x, p.device, reduce, denoise, debug, narrow, s);
+  if (st || ksplit == 1) return st;
+  return launch_splitk_reduce(p.workspace, ksplit, p.m, p.n, p.A_scales, p.B_scales, p.C, s);
 }
 
 // The mined GEMMs of several problems that share B's K-side noise and the
@@ -1112,6 +1227,13 @@ extern "C" int pb2_gemm(const pb2_gemm_params* pp, void* stream) {
   int st = set_device(pp->device);
   if (st) return st;
   return run_main_kernel(*pp, false, false, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int64_t pb2_gemm_workspace_bytes(int device, int64_t m, int64_t n, int64_t k) {
+  using namespace pb2;
+  if (m <= 0 || n <= 0 || k <= 0 || device < 0) return 0;
+  const int d = splitk_plan(device, m, n, k);
+  return d > 1 ? int64_t(d) * m * n * 4 : 0;
 }
 
 extern "C" int pb2_noisy_gemm_grouped(const pb2_grouped_gemm_params* gp, void* stream) {

@@ -380,6 +380,13 @@ def gemm(
     p.A_scales, p.B_scales, p.C = _ptr(A_scales), _ptr(B_scales), _ptr(C)
     p.skip_reduction = 1
     p.skip_denoising = 1
+    # A GEMM with too few tiles for the SMs (a decode batch) splits K; the
+    # int32 partials need a workspace, taken from torch's caching allocator
+    # (the stream-ordered allocator keeps it for the launches queued here).
+    ws_bytes = _lib.load().pb2_gemm_workspace_bytes(p.device, m, n, k)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=A.device) if ws_bytes > 0 else None
+    if ws is not None:
+        p.workspace, p.workspace_bytes = ws.data_ptr(), ws_bytes
     with torch.cuda.device(A.device):
         _lib.call("pb2_gemm", p, _stream(A.device), "gemm")
 
