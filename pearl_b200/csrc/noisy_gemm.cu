@@ -1059,9 +1059,11 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
   // 128-byte stages (128-byte swizzle) unless R = 64, where 64-byte stages
   // (64-byte swizzle) keep a transcript chunk a whole number of stages.
   const int bk = ((reduce || denoise) && p.r == 64) ? 64 : 128;
-  // The plain GEMM of a small problem (fewer than two 256-wide tiles per SM
-  // pair, e.g. a decode batch) runs 128-wide tiles, one per pair and round
-  // while they do not fill the pairs: more SMs streaming the weights.
+  // The plain GEMM of a small problem (fewer 256-wide tiles than SM pairs,
+  // e.g. a decode batch) runs 128-wide tiles: more SMs streaming the weights
+  // (a 128-wide tile issues half the MMA work per instruction, so wider
+  // problems keep 256-wide tiles).  A plain GEMM whose tiles fit one round
+  // of pairs runs one tile per pair.
   const int64_t tiles_m = (p.m + BM - 1) / BM;
   const int pairs_est = resident_pairs(p.device) ? resident_pairs(p.device) : std::max(1, sm_count(p.device) / 2);
   // A plain GEMM with too few 256 x 256 tiles splits K when the caller gave
@@ -1071,7 +1073,7 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
     ksplit = splitk_plan(p.device, p.m, p.n, p.k);
     if (ksplit > 1 && (p.workspace_bytes < int64_t(ksplit) * p.m * p.n * 4 || !al16(p.workspace))) ksplit = 1;
   }
-  const bool narrow = ksplit == 1 && !reduce && !denoise && tiles_m * ((p.n + BN - 1) / BN) < 2 * int64_t(pairs_est);
+  const bool narrow = ksplit == 1 && !reduce && !denoise && tiles_m * ((p.n + BN - 1) / BN) < int64_t(pairs_est);
   const int tn_width = narrow ? BN / 2 : BN;
   MainArgs a;
   std::memset(&a, 0, sizeof(a));
@@ -1094,7 +1096,7 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
   e.transcripts = p.transcripts;
   e.digests = p.digests;
   a.num_tiles = e.tiles_m * a.tiles_n * ksplit;  // work items
-  a.tpr = ((narrow || ksplit > 1) && a.num_tiles <= pairs_est) ? 1 : 2;
+  a.tpr = (!reduce && !denoise && a.num_tiles <= pairs_est) ? 1 : 2;
   a.ksplit = ksplit;
   a.ws = ksplit > 1 ? p.workspace : nullptr;
   a.sync = e.sync;
