@@ -459,6 +459,13 @@ typedef struct pb2_grouped_gemm_params {
   pb2_gemm_params shared;
   int64_t num_experts;
   const pb2_expert_gemm* experts; /* host array of num_experts entries */
+  /* Optional row map (no reference counterpart): row r of the stacked C is
+   * written to row c_row_index[r] of shared.C, a destination of c_rows >= m
+   * rows (rows outside it skipped) -- the slot-order write-back that follows
+   * the reference's loop (pearl_moe_experts.py:347, cache_flat[idx] = out)
+   * fused into the epilogue.  int32, device, m entries. */
+  const int32_t* c_row_index;
+  int64_t c_rows;
 } pb2_grouped_gemm_params;
 PB2_API int pb2_noisy_gemm_grouped(const pb2_grouped_gemm_params* p, void* stream);
 

@@ -98,7 +98,8 @@ class ExpertGemm(ctypes.Structure):
 
 
 class GroupedGemmParams(ctypes.Structure):
-    _fields_ = [("shared", GemmParams), ("num_experts", _i64), ("experts", ctypes.POINTER(ExpertGemm))]
+    _fields_ = [("shared", GemmParams), ("num_experts", _i64), ("experts", ctypes.POINTER(ExpertGemm)),
+                ("c_row_index", _vp), ("c_rows", _i64)]
 
 
 class TensorHashParams(ctypes.Structure):

@@ -71,6 +71,10 @@ struct MainArgs {
   // a reduction kernel sums the ranges and scales (1: no split).
   int ksplit;
   int32_t* ws;  // (ksplit, m, N) int32
+  // Grouped launch with a row map (ExpertEntry::c_rows): C's destination
+  // (c_dst_rows rows of N bf16).
+  uint16_t* c_dst;
+  long long c_dst_rows;
   SignalSync* sync;  // where a timed-out wait records its error
   const uint32_t* target;
   const uint32_t* key;
@@ -99,6 +103,9 @@ struct ExpertEntry {
   long long hit_cap;
   uint32_t* transcripts;
   uint32_t* digests;
+  // Optional: row r of this problem's C goes to row c_rows[r] of a.c_dst
+  // (the MoE slot-order write-back fused into the epilogue); null: tmC.
+  const int32_t* c_rows;
 };
 constexpr int kMaxExperts = 16;  // experts of one grouped launch (kernel parameter space)
 template <int kE>
@@ -753,7 +760,33 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (do_fold) fold32(v, p0, p1, p2, p3);
           if (h == 1) release(false);
           pack_half(v, h, pk);
-          store_c_packed(&E.tmC, box, pk, row0, tn * kTN + 64 * wi + 32 * h, lane);
+          if (kE > 1 && E.c_rows) {
+            // Row map: the block goes through the warp's shared-memory box
+            // (as for the TMA store) and out in whole 64-byte rows, eight
+            // rows per store instruction (four lanes a row), each to the row
+            // the map names; rows outside the destination are skipped.
+            const int row = row0 + lane;
+            const long long my_dr = row < E.m ? (long long)E.c_rows[row] : -1;
+            const int col = tn * kTN + 64 * wi + 32 * h;
+            uint8_t* rowp = box + lane * 64;
+            __syncwarp();  // the box's previous rows have been read
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              *reinterpret_cast<uint4*>(rowp + ((kk ^ ((lane >> 1) & 3)) << 4)) =
+                  make_uint4(pk[4 * kk], pk[4 * kk + 1], pk[4 * kk + 2], pk[4 * kk + 3]);
+            __syncwarp();
+            const int piece = lane & 3;
+#pragma unroll
+            for (int it = 0; it < 4; ++it) {
+              const int br = 8 * it + (lane >> 2);  // box row this lane moves
+              const long long dr = __shfl_sync(0xffffffffu, my_dr, br);
+              const uint4 val = *reinterpret_cast<const uint4*>(box + br * 64 + ((piece ^ ((br >> 1) & 3)) << 4));
+              if (dr >= 0 && dr < a.c_dst_rows && col + 8 * piece < a.N)
+                *reinterpret_cast<uint4*>(a.c_dst + dr * a.N + col + 8 * piece) = val;
+            }
+          } else {
+            store_c_packed(&E.tmC, box, pk, row0, tn * kTN + 64 * wi + 32 * h, lane);
+          }
         }
       } else {
         release(false);
@@ -1119,7 +1152,7 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
 // [e n, e n + n) of the B-side ones (BpEB, EARxBpEB_fp16, EBR_fp16,
 // B_scales), and signals its hits through its own buffers.
 int run_grouped_kernel(const pb2_gemm_params& p, const pb2_expert_gemm* experts, int64_t num_experts,
-                       cudaStream_t s) {
+                       const int32_t* c_row_index, int64_t c_rows, cudaStream_t s) {
   const int bk = p.r == 64 ? 64 : 128;
   const int spu = int(p.r) / bk;
   for (int64_t e0 = 0; e0 < num_experts; e0 += kMaxExperts) {
@@ -1151,6 +1184,7 @@ int run_grouped_kernel(const pb2_gemm_params& p, const pb2_expert_gemm* experts,
       e.hit_cap = q.hits ? q.hit_capacity : 0;
       e.transcripts = q.transcripts;
       e.digests = q.digests;
+      e.c_rows = c_row_index && q.m > 0 ? c_row_index + q.a_row0 : nullptr;
       if (!first_sync && q.m > 0) first_sync = e.sync;
       tiles += e.tiles_m * a.tiles_n;
     }
@@ -1159,6 +1193,8 @@ int run_grouped_kernel(const pb2_gemm_params& p, const pb2_expert_gemm* experts,
     a.num_tiles = tiles;
     a.tpr = 2;
     a.sync = first_sync;
+    a.c_dst = static_cast<uint16_t*>(p.C);
+    a.c_dst_rows = c_row_index ? c_rows : 0;
     int dev = p.device;
     if (bk == 64) st = launch_variant<64, 1, true, true, false, BN, kMaxExperts>(a, x, dev, s);
     else if (spu == 2) st = launch_variant<128, 2, true, true, false, BN, kMaxExperts>(a, x, dev, s);
@@ -1170,7 +1206,7 @@ int run_grouped_kernel(const pb2_gemm_params& p, const pb2_expert_gemm* experts,
 
 int denoise_convert(const int32_t* in, void* out, int64_t count, float scale, cudaStream_t s);
 int run_grouped_kernel(const pb2_gemm_params& p, const pb2_expert_gemm* experts, int64_t num_experts,
-                       cudaStream_t s);
+                       const int32_t* c_row_index, int64_t c_rows, cudaStream_t s);
 int run_noising_both(const pb2_noising_params& pa, const pb2_noising_params& pb, cudaStream_t stream);
 
 }  // namespace pb2
@@ -1258,6 +1294,10 @@ extern "C" int pb2_noisy_gemm_grouped(const pb2_grouped_gemm_params* gp, void* s
     next += q.m;
   }
   if (next != p.m) return PB2_ERR_INVALID_ARGUMENT;
+  // A row map sends C's rows into a destination of c_rows >= m rows (the
+  // per-expert tensor maps, unused then, still cover rows [0, m) of it).
+  if (gp->c_row_index && (gp->c_rows < p.m || reinterpret_cast<uintptr_t>(gp->c_row_index) % 4))
+    return PB2_ERR_INVALID_ARGUMENT;
   // The shared checks on the stacked problem (all rows of A, n rows of B
   // per expert): a rejected call queues no work.
   pb2_gemm_params all = p;
@@ -1288,7 +1328,7 @@ extern "C" int pb2_noisy_gemm_grouped(const pb2_grouped_gemm_params* gp, void* s
   } else if (p.run_noising_b) {
     if ((st = pb2_noise_B(&qb, stream))) return st;
   }
-  return run_grouped_kernel(p, gp->experts, E, s);
+  return run_grouped_kernel(p, gp->experts, E, gp->c_row_index, gp->c_rows, s);
 }
 
 namespace pb2 {

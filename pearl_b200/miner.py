@@ -453,7 +453,6 @@ def moe_gemm1(A_q, A_scales, topk_ids, w1, w1_scale, job: MiningJob,
         layout, A_q, A_scales, ctx.EAL, ctx.EAL_fp16)
     if out is None:
         out = torch.empty((num_tokens * top_k, N), dtype=torch.bfloat16, device=A_q.device)
-    by_slot = torch.empty_like(out)
     res = MoEGemm1Result(ctx)
     if grouped:
         # Every expert's mined GEMM in one noising and one persistent launch
@@ -473,16 +472,17 @@ def moe_gemm1(A_q, A_scales, topk_ids, w1, w1_scale, job: MiningJob,
             torch.empty((E * N, r), dtype=torch.float16, device=dev),
             torch.empty((m_all, K), dtype=torch.int8, device=dev),
             torch.empty((E * N, K), dtype=torch.int8, device=dev),
-            S_e_all.reshape(-1).contiguous(), w1_scale.reshape(-1).contiguous(), by_slot, counts, headers,
+            S_e_all.reshape(-1).contiguous(), w1_scale.reshape(-1).contiguous(), out, counts, headers,
             [syncs[e] for e in range(E)], ctx.pow_target, ctx.pow_key, hits=hits,
-            tile_size_m=config.tile_size_m, tile_size_n=config.tile_size_n, tile_size_k=config.tile_size_k)
-        # out[slot_indices] = C (pearl_moe_experts.py:347) for all experts at once
-        scatter_rows(by_slot, out, layout.slot_indices)
+            tile_size_m=config.tile_size_m, tile_size_n=config.tile_size_n, tile_size_k=config.tile_size_k,
+            # out[slot_indices] = C (pearl_moe_experts.py:347), written by the epilogue itself
+            c_row_index=layout.slot_indices)
         for e in range(E):
             if counts[e]:
                 res.per_expert[e] = MinedGemm(headers[e], syncs[e], ctx.commitment_hash_A,
                                               ctx.commitment_hash_B, hits[e] if hits else None)
         return out, res
+    by_slot = torch.empty_like(out)
     for e in range(E):
         start, count = layout.expert_slice(e)
         if count == 0:

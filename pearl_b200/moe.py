@@ -95,7 +95,7 @@ def noisy_gemm_grouped(
     AxEBL_fp16, EARxBpEB_fp16, ApEA, BpEB, A_scales, B_scales, C, expert_rows,
     host_signal_headers, host_signal_syncs, pow_target, pow_key, *, hits=None, transcripts=None,
     digests=None, run_noising_A: bool = True, run_noising_B: bool = True, tile_size_m: int = 128,
-    tile_size_n: int = 256, tile_size_k: int = 128,
+    tile_size_n: int = 256, tile_size_k: int = 128, c_row_index=None,
 ):
     """The mined GEMM1 of every expert of a MoE layer in one call: for expert
     e, exactly ``noisy_gemm`` (run_noising_A/B, reduction and denoising on) of
@@ -110,7 +110,12 @@ def noisy_gemm_grouped(
     K-side factors EAR_* / EBL_* are shared.  ``host_signal_headers`` /
     ``host_signal_syncs`` (and the optional ``hits`` / ``transcripts`` /
     ``digests``) are per-expert lists, used as for that expert's own
-    noisy_gemm."""
+    noisy_gemm.
+
+    ``c_row_index`` (optional, int32 (m,) on the device) fuses the slot-order
+    write-back that follows the reference's loop (pearl_moe_experts.py:347,
+    ``cache_flat[idx] = out``) into the epilogue: row i of the experts' C
+    goes to row c_row_index[i] of ``C``, which then has at least m rows."""
     from .pearl_gemm_interface import _check_matmul_config, _check_tensor, _gemm_params, _ptr
 
     E = len(expert_rows)
@@ -129,7 +134,8 @@ def noisy_gemm_grouped(
             (A, (m, k), torch.int8, "A"), (EAL, (m, r), torch.int8, "EAL"),
             (EAL_fp16, (m, r), torch.float16, "EAL_fp16"), (ApEA, (m, k), torch.int8, "ApEA"),
             (AxEBL_fp16, (m, r), torch.float16, "AxEBL_fp16"), (A_scales, (m,), torch.float32, "A_scales"),
-            (C, (m, n), torch.bfloat16, "C"), (B, (n_all, k), torch.int8, "B"),
+            (C, (C.shape[0] if c_row_index is not None else m, n), torch.bfloat16, "C"),
+            (B, (n_all, k), torch.int8, "B"),
             (EBR, (n_all, r), torch.int8, "EBR"), (EBR_fp16, (n_all, r), torch.float16, "EBR_fp16"),
             (BpEB, (n_all, k), torch.int8, "BpEB"), (EARxBpEB_fp16, (n_all, r), torch.float16, "EARxBpEB_fp16"),
             (B_scales, (n_all,), torch.float32, "B_scales"), (EAR_R_major, (k, r), torch.int8, "EAR_R_major"),
@@ -138,6 +144,10 @@ def noisy_gemm_grouped(
         _check_tensor(t, shape, dt, name)
     for t, name in ((pow_target, "pow_target"), (pow_key, "pow_key")):
         _check_tensor(t, (8,), torch.uint32, name)
+    if c_row_index is not None:
+        _check_tensor(c_row_index, (m,), torch.int32, "c_row_index")
+        if C.shape[0] < m:
+            _fail(f"C must have at least {m} rows with c_row_index")
     if len(host_signal_headers) != E or len(host_signal_syncs) != E:
         _fail("one host signal header and one sync buffer per expert")
     p = _gemm_params(m, n, k, r, _device_index(A), tile_size_m, tile_size_n, tile_size_k, 1, 1, None, None,
@@ -175,5 +185,7 @@ def noisy_gemm_grouped(
                 setattr(q, field, _ptr(lst[e]))
     g = _lib.GroupedGemmParams()
     g.shared, g.num_experts, g.experts = p, E, table
+    if c_row_index is not None:
+        g.c_row_index, g.c_rows = _ptr(c_row_index), C.shape[0]
     with torch.cuda.device(A.device):
         _lib.call("pb2_noisy_gemm_grouped", g, _stream(A.device), "noisy_gemm_grouped")

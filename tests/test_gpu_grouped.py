@@ -136,3 +136,36 @@ def test_grouped_rejects_bad_expert_rows():
         moe.noisy_gemm_grouped(*args, [64, 32], hdr, sync, target, t["pow_key"])  # rows do not add up
     with pytest.raises(RuntimeError):
         moe.noisy_gemm_grouped(*args, [64, 64], hdr[:1], sync[:1], target, t["pow_key"])
+
+
+def test_grouped_row_map_writes_c_in_slot_order():
+    """c_row_index fuses the slot-order write-back (pearl_moe_experts.py:347,
+    cache_flat[idx] = out) into the epilogue: the destination gets exactly
+    the rows the unmapped launch writes, moved by the index, and rows no
+    index names are left alone; hits and sync words are unchanged."""
+    counts, n, k, r = [300, 0, 17, 129, 5, 1000], 384, 768, 128
+    E, m = len(counts), sum(counts)
+    t = _problem(counts, n, k, r, seed=77)
+    target = pg.make_pow_target_tensor(1 << 251)
+    g = torch.Generator().manual_seed(5)
+    idx = torch.randperm(m + 7, generator=g)[:m].to(torch.int32).cuda()
+
+    def run(row_map):
+        o = _outs(m, E * n, k, r, n)
+        sync = [torch.zeros(16, dtype=torch.int8, device="cuda") for _ in range(E)]
+        hdr = [torch.zeros(640, dtype=torch.int8).pin_memory() for _ in range(E)]
+        dst = torch.full((m + 7, n), 3.0, dtype=torch.bfloat16, device="cuda") if row_map else o["C"]
+        moe.noisy_gemm_grouped(
+            t["A"], t["B"], t["EAL"], t["EAL_fp16"], t["EBR"], t["EBR_fp16"], t["EAR_R_major"],
+            t["EBL_R_major"], t["EAR_K_major"], t["EBL_K_major"], o["AxEBL_fp16"], o["EARxBpEB_fp16"],
+            o["ApEA"], o["BpEB"], t["A_scales"], t["B_scales"], dst, counts, hdr, sync, target, t["pow_key"],
+            c_row_index=idx if row_map else None)
+        torch.cuda.synchronize()
+        return dst, [pg.get_host_signal_sync_fields(s) for s in sync]
+
+    plain, f_plain = run(False)
+    mapped, f_mapped = run(True)
+    assert f_plain == f_mapped
+    want = torch.full((m + 7, n), 3.0, dtype=torch.bfloat16, device="cuda")
+    want[idx.long()] = plain
+    assert torch.equal(mapped, want)
