@@ -412,8 +412,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (kDenoise) {
-          for (int d = 0; d < nden && ok; ++d) {
-            for (int s = 0; s < (two ? 2 : 1) && ok; ++s) {
+          for (int s = 0; s < (two ? 2 : 1) && ok; ++s) {
+            for (int d = 0; d < nden && ok; ++d) {
               const int m0 = s ? mb : ma, n0 = s ? nb : na;
               const ExpertEntry& Es = s ? Eb : Ea;
               for (int st = 0; st < stages_per_unit; ++st, ++it) {
@@ -482,8 +482,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // With the transcript every unit is a fold event, and the stage's
         // commit above doubles as "accumulator ready" (one commit per unit
-        // keeps the tensor pipe's queue full).  A lone event gets its own.
-        if (!kReduce && u == nmain - 1) umma_commit_2sm_warp(&S.acc_full[s], kPairMask);
+        // keeps the tensor pipe's queue full).  A tile's last unit gets its
+        // own commit: its stage is refilled by the denoise units of the
+        // other slot, which do not wait for this slot's event.
+        if (u == nmain - 1) umma_commit_2sm_warp(&S.acc_full[s], kPairMask);
         if (kReduce || u == nmain - 1) pend |= 1u << s;
       };
       auto denoise_unit = [&](int s, int d) {
@@ -510,11 +512,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           main_unit(0, u);
           if (two && ok) main_unit(1, u);
         }
+        // Each slot's denoise units back to back: slot 0's run while the fold
+        // warps still rewrite slot 1's accumulator as f32.
         if (kDenoise) {
-          for (int d = 0; d < nden && ok; ++d) {
-            denoise_unit(0, d);
-            if (two && ok) denoise_unit(1, d);
-          }
+          for (int d = 0; d < nden && ok; ++d) denoise_unit(0, d);
+          if (two)
+            for (int d = 0; d < nden && ok; ++d) denoise_unit(1, d);
         }
       }
       // Every MMA has retired before TMEM is released.
@@ -562,8 +565,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the issue order than the stage's previous use -- and if the phase
     // cannot be overtaken, which it cannot: the issuer reuses the slot, and
     // so comes within kStages units of refilling the stage, only after these
-    // warps release it.  Lone events (the f32 rewrite without a transcript,
-    // the final store) have no such neighbour and wait on acc_full instead.
+    // warps release it.  A tile's last chunk has no such guarantee (slot 0's
+    // denoise units refill slot 1's last stage without waiting for slot 1's
+    // event), so it and the final store wait on the slot's acc_full commit.
     auto fold_slot = [&](auto slot, int round, int u, const TileRef& tr, uint32_t last_stage) {
       const int tm = tr.tm, tn = tr.tn;
       const ExpertEntry& E = x.ex[tr.e];
@@ -571,7 +575,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int b = 2 * s + (round & 1);  // transcript buffer
       const bool is_main = u < nmain;
       const bool last_main = u == nmain - 1;
-      if (kReduce && is_main) {
+      if (kReduce && is_main && !last_main) {
         if (!(ok = mbar_wait_warp(&S.empty[last_stage % kStages], (last_stage / kStages) & 1, abort_flag, a.sync,
                                   a.wait_budget)))
           return;
