@@ -7,7 +7,9 @@
 // factor matrices:
 //   XpE  = int8(X + EL . E_rmajor^T)       (EA = EAL . EAR, EB = EBR . EBL)
 //   proj = Xs . E_kmajor^T                 (Xs = X for noise_A, XpE for noise_B)
-// One CTA owns 256 rows of X and a range of 128-wide k-blocks.  Per k-block
+// One CTA owns nm <= 256 rows of X and a range of 128-wide k-blocks (rows of
+// the 256-row MMA tile past nm hold stale shared memory: they are computed
+// and never stored).  Per k-block
 // the MMA warp computes D1 = EL . E_rmajor[kb]^T (256 x 128 int32, K = r, as
 // two 128-row MMAs sharing the E tile) into TMEM and accumulates
 // D2 += Xs[kb] . E_kmajor[kb]^T (256 x r int32).  Sixteen epilogue warps add
@@ -29,7 +31,7 @@
 namespace pb2 {
 namespace {
 
-constexpr int NM = 256;  // rows of X per CTA (two 128-row MMA halves)
+constexpr int NM = 256;  // most rows of X per CTA (two 128-row MMA halves); NoisingArgs::nm <= NM
 constexpr int NKB = 128; // k per k-block
 constexpr int kEpiWarps = 16;  // per TMEM lane quadrant: 2 row halves x 2 column halves
 constexpr int kThreads = 32 * (2 + kEpiWarps);  // TMA, MMA, 8 epilogue
@@ -42,6 +44,7 @@ constexpr int kSmemPlan = kElBytes + kStages * kStageSlot;
 struct NoisingArgs {
   CUtensorMap tmX, tmEL, tmE1, tmE2;
   int rows, K, nkb, kbps, ks;
+  int nm;  // rows of X per CTA: a multiple of 8, at most NM (the TMA boxes of X and EL are nm rows high)
   int use_cluster;
   int proj_fp16;
   float scale;
@@ -135,7 +138,7 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int kb0 = blockIdx.y * a.kbps;
   const int nkb = min(a.kbps, a.nkb - kb0);
-  const int r0 = blockIdx.x * NM;
+  const int r0 = blockIdx.x * a.nm;
   const uint32_t rank = a.use_cluster ? cluster_ctarank() : 0;
   bool waited_cluster = false;
 
@@ -181,7 +184,7 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
         tma_prefetch(&a.tmX);
         tma_prefetch(&a.tmE1);
         tma_prefetch(&a.tmE2);
-        mbar_arrive_expect_tx(&S.el_full, NM * R);
+        mbar_arrive_expect_tx(&S.el_full, a.nm * R);
         tma_load_2d(&a.tmEL, &S.el_full, el_buf, 0, r0);
       }
       int i = 0;
@@ -195,7 +198,7 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
           mbar_arrive_expect_tx(&S.full_e[s], kE1Bytes + kE2Bytes);
           tma_load_2d(&a.tmE1, &S.full_e[s], st + kXBytes, 0, k);
           tma_load_2d(&a.tmE2, &S.full_e[s], st + kXBytes + 16384, k, 0);
-          mbar_arrive_expect_tx(&S.full_x[s], kXBytes);
+          mbar_arrive_expect_tx(&S.full_x[s], a.nm * NKB);
           tma_load_2d(&a.tmX, &S.full_x[s], st, k, r0);
         }
       }
@@ -323,7 +326,7 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
           const int rr = 128 * h + 32 * q + 8 * j + (sub >> 1) + 4 * (sub & 1);
           const uint4 val = *reinterpret_cast<const uint4*>(xt + sw128_off(rr, ch));
           const int64_t g = int64_t(r0) + rr;
-          if (g < a.rows && kc < a.K) *reinterpret_cast<uint4*>(a.XpE + g * a.K + kc) = val;
+          if (rr < a.nm && g < a.rows && kc < a.K) *reinterpret_cast<uint4*>(a.XpE + g * a.K + kc) = val;
         }
       }
       __syncwarp();
@@ -374,8 +377,8 @@ __device__ __forceinline__ void noising_body(const NoisingArgs& a) {
                          : mbar_wait_warp(&S.red_ready, 0, abort_flag, a.sync, a.wait_budget);
     }
     if (ok) {
-      const int per = (NM + nr - 1) / nr;
-      const int lo = int(rank) * per, hi = min(NM, lo + per);
+      const int per = (a.nm + nr - 1) / nr;
+      const int lo = int(rank) * per, hi = min(a.nm, lo + per);
       const int sub = lane / kChunks, cl = lane % kChunks;
       constexpr int kStep = kEpiWarps * kRowsPerIter;  // rows between a thread's rows
       // Two rows per pass with every rank's partial of both in flight (one
@@ -454,9 +457,9 @@ template <int R>
 __global__ void __launch_bounds__(kThreads, 1)
     noising_pair_kernel(const __grid_constant__ NoisingArgs a, const __grid_constant__ NoisingArgs b) {
   if (blockIdx.z == 0) {
-    if (int(blockIdx.x) * NM < a.rows) noising_body<R, false>(a);
+    if (int(blockIdx.x) * a.nm < a.rows) noising_body<R, false>(a);
   } else {
-    if (int(blockIdx.x) * NM < b.rows) noising_body<R, true>(b);
+    if (int(blockIdx.x) * b.nm < b.rows) noising_body<R, true>(b);
   }
 }
 
@@ -516,8 +519,36 @@ int max_active_clusters(int device, int ks) {
   return n;
 }
 
+// Rows of X per CTA: the tensor maps of X and EL load boxes nm rows high.
+int set_rows_per_block(NoisingArgs& a, const pb2_noising_params& p, int nm) {
+  const CUtensorMapSwizzle rswz = p.r == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  int st;
+  if ((st = make_tmap_2d(&a.tmX, p.X, U8, 1, p.k, p.rows, NKB, nm, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (st = make_tmap_2d(&a.tmEL, p.EL, U8, 1, int(p.r), p.rows, int(p.r), nm, rswz)))
+    return st;
+  a.nm = nm;
+  return PB2_OK;
+}
+
+// The smallest row block (a multiple of 8 in [128, NM]) whose blocks, for
+// operands of rows_a and rows_b rows, still run as one wave of ks-CTA
+// clusters: more of the SMs stream X, each with less of it (at 8192 rows per
+// operand and ks = 2: 224-row blocks, 148 CTAs, against 128 CTAs of 256).
+int rows_per_block(int device, int64_t rows_a, int64_t rows_b, int ks) {
+  const int sms = std::max(1, sm_count(device));
+  int cap = sms / std::max(1, ks);
+  if (ks > 1) {
+    const int fit = max_active_clusters(device, ks);
+    if (fit >= 0) cap = std::min(cap, fit);
+  }
+  for (int nm = 128; nm < NM; nm += 8)
+    if ((rows_a + nm - 1) / nm + (rows_b + nm - 1) / nm <= cap) return nm;
+  return NM;
+}
+
 // Validates one operand's parameters and fills its arguments except the K
-// split (kbps, ks, use_cluster).
+// split (kbps, ks, use_cluster); the row block is NM until a caller sets it.
 int prepare_noising(const pb2_noising_params& p, bool b_side, NoisingArgs* out) {
   if (!p.X || !p.EL || !p.E_rmajor || !p.E_kmajor || !p.XpE || !p.proj)
     return PB2_ERR_INVALID_ARGUMENT;
@@ -535,8 +566,7 @@ int prepare_noising(const pb2_noising_params& p, bool b_side, NoisingArgs* out) 
   NoisingArgs& a = *out;
   std::memset(&a, 0, sizeof(a));
   const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
-  if ((st = make_tmap_2d(&a.tmX, p.X, U8, 1, p.k, p.rows, NKB, NM, CU_TENSOR_MAP_SWIZZLE_128B)) ||
-      (st = make_tmap_2d(&a.tmEL, p.EL, U8, 1, r, p.rows, r, NM, rswz)) ||
+  if ((st = set_rows_per_block(a, p, NM)) ||
       (st = make_tmap_2d(&a.tmE1, p.E_rmajor, U8, 1, r, p.k, r, NKB, rswz)) ||
       (st = make_tmap_2d(&a.tmE2, p.E_kmajor, U8, 1, p.k, r, NKB, r, CU_TENSOR_MAP_SWIZZLE_128B)))
     return st;
@@ -580,11 +610,13 @@ int run_noising(const pb2_noising_params& p, bool b_side, cudaStream_t stream) {
   NoisingArgs a;
   int st = prepare_noising(p, b_side, &a);
   if (st) return st;
-  const int row_blocks = int((p.rows + NM - 1) / NM);
+  int row_blocks = int((p.rows + NM - 1) / NM);
   const int sms = std::max(1, sm_count(p.device));
   int ks;
   if (p.proj_is_fp16) {
     ks = fp16_split(p.device, row_blocks, a.nkb);
+    if ((st = set_rows_per_block(a, p, rows_per_block(p.device, p.rows, 0, ks)))) return st;
+    row_blocks = int((p.rows + a.nm - 1) / a.nm);
   } else if (p.k_blocks_per_split > 0) {
     ks = (a.nkb + p.k_blocks_per_split - 1) / p.k_blocks_per_split;
   } else if (p.k_blocks_per_split == 0) {
@@ -639,11 +671,12 @@ int run_noising_both(const pb2_noising_params& pa, const pb2_noising_params& pb,
   NoisingArgs a, b;
   int st = prepare_noising(pa, false, &a);
   if (st || (st = prepare_noising(pb, true, &b))) return st;
-  const int rba = int((pa.rows + NM - 1) / NM), rbb = int((pb.rows + NM - 1) / NM);
-  const int ks = fp16_split(pa.device, rba + rbb, a.nkb);
+  const int ks = fp16_split(pa.device, int((pa.rows + NM - 1) / NM + (pb.rows + NM - 1) / NM), a.nkb);
+  const int nm = rows_per_block(pa.device, pa.rows, pb.rows, ks);
+  if ((st = set_rows_per_block(a, pa, nm)) || (st = set_rows_per_block(b, pb, nm))) return st;
   set_split(a, ks);
   set_split(b, ks);
-  const int rb = std::max(rba, rbb);
+  const int rb = int(std::max((pa.rows + nm - 1) / nm, (pb.rows + nm - 1) / nm));
   return pa.r == 128 ? launch_noising_pair<128>(a, b, rb, stream) : launch_noising_pair<64>(a, b, rb, stream);
 }
 

@@ -121,6 +121,26 @@ def test_noise_AB_matches_noise_A_and_noise_B(m, n, k, r, dtype):
         assert np.array_equal(_np(earx), (o.EARxBpEB.astype(np.float32) * 2.0 ** -12).astype(np.float16))
 
 
+@pytest.mark.parametrize("m,n,k", [(8192, 8192, 1024), (16384, 8192, 512), (8000, 1000, 768)])
+def test_noise_AB_row_blocks_below_256(m, n, k):
+    """Large operands run with row blocks shorter than the 256-row MMA tile,
+    so that every SM streams X (8192 + 8192 rows: 224-row blocks, the last
+    one ragged; 16384 + 8192: 168-row blocks).  Rows of the tile past the
+    block are computed and never stored: the outputs must still be the
+    oracle's bytes."""
+    p = make_problem(m, n, k, 128, seed=17)
+    gen_noise(p)
+    o = oracle_problem(p)
+    axebl = torch.zeros(m, 128, dtype=torch.float16, device="cuda")
+    earx = torch.zeros(n, 128, dtype=torch.float16, device="cuda")
+    pg.noise_AB(p.A, p.noise["EAL"], axebl, p.out["ApEA"], p.B, p.noise["EBR"], earx, p.out["BpEB"],
+                **{k_: v for k_, v in p.noise.items() if k_ not in ("EAL", "EBR")})
+    assert np.array_equal(_np(p.out["ApEA"]), o.ApEA)
+    assert np.array_equal(_np(p.out["BpEB"]), o.BpEB)
+    assert np.array_equal(_np(axebl), (o.AxEBL.astype(np.float32) * 2.0 ** -14).astype(np.float16))
+    assert np.array_equal(_np(earx), (o.EARxBpEB.astype(np.float32) * 2.0 ** -12).astype(np.float16))
+
+
 def test_denoise_converter_bit_exact():
     g = torch.Generator().manual_seed(4)
     a = torch.randint(-30000, 30000, (512, 128), generator=g, dtype=torch.int32)
