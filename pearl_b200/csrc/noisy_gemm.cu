@@ -71,6 +71,7 @@ struct MainArgs {
   // a reduction kernel sums the ranges and scales (1: no split).
   int ksplit;
   int32_t* ws;  // (ksplit, m, N) int32
+  CUtensorMap tmW;  // ws as (N, m, ksplit) int32, 16 x 32 boxes, 64-byte swizzle (split-K only)
   // Grouped launch with a row map (ExpertEntry::c_rows): C's destination
   // (c_dst_rows rows of N bf16).
   uint16_t* c_dst;
@@ -264,6 +265,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kStageBudget = stage_budget(kReduce);
   constexpr int kStages =
       (kStageBudget / kStageBytes) < kMaxStages ? (kStageBudget / kStageBytes) : kMaxStages;
+  // Split-K partials can be staged in the idle operand ring: 8 KB per fold warp.
+  constexpr bool kRingStagesPartials = kStages * kStageBytes >= kFoldWarps * 8192;
   static_assert(kStageBudget + (kReduce ? kXbufBytes : 0) + kCStageBytes + 1024 + 256 <= 232448,
                 "shared memory plan exceeds 227 KB");
   constexpr uint32_t kIdescI8 =
@@ -755,10 +758,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       if (strip_live && !kReduce && !kDenoise && a.ksplit > 1) {
-        // A split-K item: this lane's row of the exact int32 partial goes to
-        // ws[ks] as it is (whole 16-byte vectors: N % 8 == 0); the reduction
-        // kernel sums the ranges and scales.
-        const int row = tm * BM + int(rank) * BMC + 32 * q + lane;
+        // A split-K item: this warp's 32 x 64 block of the exact int32
+        // partial goes to ws[ks] as it is; the reduction kernel sums the
+        // ranges and scales.  After the CTA's last item the operand ring is
+        // idle (every stage has been consumed by the MMAs this event waited
+        // for), so the block is staged there as four 16-column boxes and
+        // leaves by TMA stores (whole lines, rows >= m clipped within the
+        // slab); otherwise it is stored from registers, 16 bytes per lane.
+        const int row0 = tm * BM + int(rank) * BMC + 32 * q;
+        const int row = row0 + lane;
+        const bool staged = kRingStagesPartials && first + (round + 1) * stride >= a.num_tiles;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           uint32_t v[32];
@@ -767,7 +776,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_ld_into(v);
           if (h == 1) release(false);
           const int col = tn * kTN + 64 * wi + 32 * h;
-          if (row < E.m) {
+          if (staged) {
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+              uint8_t* box = stage_mem + fw * 8192 + (2 * h + p) * 2048;
+              uint8_t* rowp = box + lane * 64;
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                *reinterpret_cast<uint4*>(rowp + ((k ^ ((lane >> 1) & 3)) << 4)) =
+                    make_uint4(v[16 * p + 4 * k], v[16 * p + 4 * k + 1], v[16 * p + 4 * k + 2], v[16 * p + 4 * k + 3]);
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_3d(&a.tmW, box, col + 16 * p, row0, tr.ks);
+                bulk_commit_group();
+              }
+            }
+          } else if (row < E.m) {
             int32_t* dst = a.ws + (int64_t(tr.ks) * E.m + row) * int64_t(a.N) + col;
 #pragma unroll
             for (int j = 0; j < 8; ++j)
@@ -1159,6 +1184,9 @@ int run_main_kernel(const pb2_gemm_params& p, bool reduce, bool denoise, cudaStr
   a.tpr = (!reduce && !denoise && a.num_tiles <= pairs_est) ? 1 : 2;
   a.ksplit = ksplit;
   a.ws = ksplit > 1 ? p.workspace : nullptr;
+  if (ksplit > 1 && (st = make_tmap_3d(&a.tmW, p.workspace, CU_TENSOR_MAP_DATA_TYPE_INT32, 4, p.n, p.m, ksplit, 16, 32,
+                                       CU_TENSOR_MAP_SWIZZLE_64B)))
+    return st;
   a.sync = e.sync;
 
   // Operand stages per unit: a unit is R bytes of K with transcript or

@@ -180,6 +180,13 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
                "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
 }
+// 3-D form (box of depth 1 at {x, y, z}).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
@@ -790,6 +797,9 @@ struct NvtxRange {
 };
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
                  uint64_t inner, uint64_t outer, uint32_t box_inner, uint32_t box_outer,
+                 CUtensorMapSwizzle swizzle);
+int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
+                 uint64_t inner, uint64_t mid, uint64_t outer, uint32_t box_inner, uint32_t box_mid,
                  CUtensorMapSwizzle swizzle);
 int set_device(int device);
 int sm_count(int device);

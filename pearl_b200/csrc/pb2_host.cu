@@ -65,6 +65,30 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
   return PB2_OK;
 }
 
+// 3-D tiled map (dims inner, mid, outer; row-major, no padding): each
+// dimension clips on its own, so a box never crosses into the next slab.
+int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
+                 uint64_t inner, uint64_t mid, uint64_t outer, uint32_t box_inner, uint32_t box_mid,
+                 CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return PB2_ERR_NO_DRIVER_ENTRY;
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return PB2_ERR_INVALID_ARGUMENT;
+  if ((inner * elem_bytes) % 16 != 0) return PB2_ERR_INVALID_ARGUMENT;
+  cuuint64_t dims[3] = {inner, mid, outer};
+  cuuint64_t strides[2] = {inner * elem_bytes, inner * mid * elem_bytes};
+  cuuint32_t box[3] = {box_inner, box_mid, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dtype, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    std::snprintf(g_last_cuda_error, sizeof(g_last_cuda_error),
+                  "cuTensorMapEncodeTiled failed (%d)", int(r));
+    return PB2_ERR_INVALID_ARGUMENT;
+  }
+  return PB2_OK;
+}
+
 int set_device(int device) { return note_cuda(cudaSetDevice(device)); }
 
 int sm_count(int device) {
