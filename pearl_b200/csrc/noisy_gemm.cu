@@ -81,6 +81,7 @@ struct MainArgs {
   const uint32_t* key;
   unsigned long long* counter;
   long long wait_budget;  // SM cycles a device-side wait may spin (pb2_set_wait_budget_cycles)
+  uint32_t wait_hint_ns;  // suspend hint of those waits, derived from the budget (suspend_hint_ns)
 };
 
 // One GEMM of the launch: the whole problem of pb2_noisy_gemm, or one expert
@@ -423,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const CUtensorMap* tmA = s ? &Eb.tmA : &Ea.tmA;
             for (int st = 0; st < stages_per_unit; ++st, ++it) {
               const int j = it % kStages;
-              if (!(ok = mbar_wait_warp(&S.empty[j], ((it / kStages) & 1) ^ 1, abort_flag, a.sync, a.wait_budget))) break;
+              if (!(ok = mbar_wait_warp(&S.empty[j], ((it / kStages) & 1) ^ 1, abort_flag, a.sync, a.wait_budget, a.wait_hint_ns))) break;
               uint8_t* sa = stage_mem + j * kStageBytes;
               const int kbyte = (kbase + u) * unit_k + st * BK;
               if (leader) {
@@ -442,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const ExpertEntry& Es = s ? Eb : Ea;
               for (int st = 0; st < stages_per_unit; ++st, ++it) {
                 const int j = it % kStages;
-                if (!(ok = mbar_wait_warp(&S.empty[j], ((it / kStages) & 1) ^ 1, abort_flag, a.sync, a.wait_budget))) break;
+                if (!(ok = mbar_wait_warp(&S.empty[j], ((it / kStages) & 1) ^ 1, abort_flag, a.sync, a.wait_budget, a.wait_hint_ns))) break;
                 uint8_t* sa = stage_mem + j * kStageBytes;
                 const int ds = d * stages_per_unit + st;
                 const int col = (ds % den_stages_per_product) * (BK / 2);
@@ -485,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t sbase = smem_u32(stage_mem);
       auto acquire = [&](int s) -> bool {
         if (!bit(pend, s)) return true;
-        if (!mbar_wait_warp(&S.acc_empty[s], bit(empar, s), abort_flag, a.sync, a.wait_budget)) return false;
+        if (!mbar_wait_warp(&S.acc_empty[s], bit(empar, s), abort_flag, a.sync, a.wait_budget, a.wait_hint_ns)) return false;
         empar ^= 1u << s;
         pend &= ~(1u << s);
         tc_fence_after();
@@ -493,12 +494,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       auto main_unit = [&](int s, int u) {
         // Operands first (usually resident already), then the slot.
-        if (!(ok = mbar_wait_warp(&S.full[it % kStages], (it / kStages) & 1, abort_flag, a.sync, a.wait_budget))) return;
+        if (!(ok = mbar_wait_warp(&S.full[it % kStages], (it / kStages) & 1, abort_flag, a.sync, a.wait_budget, a.wait_hint_ns))) return;
         if ((kReduce || u == 0) && !(ok = acquire(s))) return;
         const uint32_t dt = tmem + 256 * s;
         for (int st = 0; st < stages_per_unit; ++st, ++it) {
           const int j = it % kStages;
-          if (st > 0 && !(ok = mbar_wait_warp(&S.full[j], (it / kStages) & 1, abort_flag, a.sync, a.wait_budget))) return;
+          if (st > 0 && !(ok = mbar_wait_warp(&S.full[j], (it / kStages) & 1, abort_flag, a.sync, a.wait_budget, a.wait_hint_ns))) return;
           tc_fence_after();
           const uint64_t ad = sdesc_kmajor<BK>(sbase + j * kStageBytes);
           const uint64_t bd = sdesc_kmajor<BK>(sbase + j * kStageBytes + kAStage);
@@ -517,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t dt = tmem + 256 * s;
         for (int st = 0; st < stages_per_unit; ++st, ++it) {
           const int j = it % kStages;
-          if (!(ok = mbar_wait_warp(&S.full[j], (it / kStages) & 1, abort_flag, a.sync, a.wait_budget))) return;
+          if (!(ok = mbar_wait_warp(&S.full[j], (it / kStages) & 1, abort_flag, a.sync, a.wait_budget, a.wait_hint_ns))) return;
           tc_fence_after();
           const uint64_t ad = sdesc_kmajor<BK>(sbase + j * kStageBytes);
           const uint64_t bd = sdesc_kmajor<BK>(sbase + j * kStageBytes + kAStage);
@@ -601,10 +602,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool last_main = u == nmain - 1;
       if (kReduce && is_main && !last_main) {
         if (!(ok = mbar_wait_warp(&S.empty[last_stage % kStages], (last_stage / kStages) & 1, abort_flag, a.sync,
-                                  a.wait_budget)))
+                                  a.wait_budget, a.wait_hint_ns)))
           return;
       } else {
-        if (!(ok = mbar_wait_warp(&S.acc_full[s], bit(fpar, s), abort_flag, a.sync, a.wait_budget))) return;
+        if (!(ok = mbar_wait_warp(&S.acc_full[s], bit(fpar, s), abort_flag, a.sync, a.wait_budget, a.wait_hint_ns))) return;
         fpar ^= 1u << s;
       }
       tc_fence_after();
@@ -648,7 +649,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // A tile's first chunk reuses the buffer of two rounds ago: the hash
         // warps must have cleared it.
         if (u == 0 && round >= 2 &&
-            !(ok = mbar_wait_idle_warp(&S.xfree[b], ((round >> 1) - 1) & 1, abort_flag, a.sync, a.wait_budget)))
+            !(ok = mbar_wait_idle_warp(&S.xfree[b], ((round >> 1) - 1) & 1, abort_flag, a.sync, a.wait_budget, a.wait_hint_ns)))
           return false;
         uint32_t* tw = xbuf + b * (16 * 256) + w * 256 + lane_tile;
         atomicXor(tw, __funnelshift_l(p0, p0, rot));
@@ -875,7 +876,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int tm = tr.tm, tn = tr.tn;
       const ExpertEntry& E = x.ex[tr.e];
       const int b = 2 * decltype(slot)::value + (round & 1);
-      if (!(ok = mbar_wait_idle_warp(&S.xready[b], (round >> 1) & 1, abort_flag, a.sync, a.wait_budget))) return;
+      if (!(ok = mbar_wait_idle_warp(&S.xready[b], (round >> 1) & 1, abort_flag, a.sync, a.wait_budget, a.wait_hint_ns))) return;
       const int tm128 = 2 * tm + int(rank);
 #pragma unroll 1
       for (int i = 0; i < 4; ++i) {
@@ -1040,6 +1041,7 @@ int make_shared_args(MainArgs& a, const pb2_gemm_params& p, int bk, int tn_width
   a.key = p.pow_key;
   a.counter = reinterpret_cast<unsigned long long*>(p.inner_hash_counter);
   a.wait_budget = wait_budget_cycles();
+  a.wait_hint_ns = suspend_hint_ns(a.wait_budget);
   return PB2_OK;
 }
 

@@ -94,26 +94,40 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 // waiting for a slot release starved the fold warps on its own
 // sub-partition, which held the release back by ~1500 cycles per R-chunk.
 constexpr uint32_t kSuspendNs = 1000000;
-__device__ __forceinline__ bool mbar_test_suspend(uint64_t* bar, uint32_t parity) {
+// The hint for a wait bounded by `budget` cycles: a quarter of the budget in
+// nanoseconds (at ~2 cycles per ns), at most kSuspendNs.  A suspended
+// try_wait returns only when the phase completes or its hint expires, and
+// the budget is checked between try_waits, so a hint longer than the budget
+// would let a short budget go unenforced.
+__host__ __device__ constexpr uint32_t suspend_hint_ns(long long budget) {
+  return budget / 4 >= (long long)kSuspendNs ? kSuspendNs : uint32_t(budget / 4 > 0 ? budget / 4 : 1);
+}
+__device__ __forceinline__ bool mbar_test_suspend(uint64_t* bar, uint32_t parity, uint32_t hint_ns = kSuspendNs) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
       : "memory");
   return ok != 0;
 }
 // Bounded wait for the phase with the given parity.  Returns false (and
 // records the error / raises the CTA abort flag) if the budget runs out or
-// another warp of the CTA already aborted.
+// another warp of the CTA already aborted.  The first check is a plain
+// try_wait (it may sleep for a system-defined time, short next to any
+// budget a caller sets: measured, a hinted or non-blocking first check
+// slowed the mined GEMM by 0.5-1.5%); every later try_wait carries hint_ns,
+// so a wait that outlasts the first check meets the budget at least every
+// hint_ns.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          SignalSync* sync, long long budget = kWaitBudgetCycles) {
+                                          SignalSync* sync, long long budget = kWaitBudgetCycles,
+                                          uint32_t hint_ns = kSuspendNs) {
   if (mbar_test(bar, parity)) return true;
   long long t0 = clock64();
   while (true) {
-    if (mbar_test_suspend(bar, parity)) return true;
+    if (mbar_test_suspend(bar, parity, hint_ns)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > budget) {
       *abort_flag = 1;
@@ -126,19 +140,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // mbar_wait by every lane of a converged warp, with one verdict for all of
 // them (a lane that ran out of budget makes the whole warp give up).
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                               SignalSync* sync, long long budget = kWaitBudgetCycles) {
-  const bool ok = mbar_wait(bar, parity, abort_flag, sync, budget);
+                                               SignalSync* sync, long long budget = kWaitBudgetCycles,
+                                               uint32_t hint_ns = kSuspendNs) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, sync, budget, hint_ns);
   return __all_sync(0xffffffffu, ok);
 }
 
 // Bounded wait for warps that may idle a long time (the same suspending
 // wait; kept as its own name for the warps whose waits are long by design).
 __device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                               SignalSync* sync, long long budget = kWaitBudgetCycles) {
+                                               SignalSync* sync, long long budget = kWaitBudgetCycles,
+                                               uint32_t hint_ns = kSuspendNs) {
   if (mbar_test(bar, parity)) return true;
   long long t0 = clock64();
   while (true) {
-    if (mbar_test_suspend(bar, parity)) return true;
+    if (mbar_test_suspend(bar, parity, hint_ns)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > budget) {
       *abort_flag = 1;
@@ -153,8 +169,9 @@ __device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity, v
 // __syncwarp, shuffles) wait with a warp-wide verdict, so a lane whose budget
 // ran out a moment before its neighbours' cannot split the warp.
 __device__ __forceinline__ bool mbar_wait_idle_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                                    SignalSync* sync, long long budget = kWaitBudgetCycles) {
-  const bool ok = mbar_wait_idle(bar, parity, abort_flag, sync, budget);
+                                                    SignalSync* sync, long long budget = kWaitBudgetCycles,
+                                                    uint32_t hint_ns = kSuspendNs) {
+  const bool ok = mbar_wait_idle(bar, parity, abort_flag, sync, budget, hint_ns);
   return __all_sync(0xffffffffu, ok);
 }
 

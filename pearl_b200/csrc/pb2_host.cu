@@ -130,9 +130,9 @@ __global__ void wait_selftest_kernel(SignalSync* sync, long long budget) {
   volatile int mine = 0;
   bool ok;
   if (warp == 0)
-    ok = mbar_wait_warp(&never[0], 0, &mine, sync, budget);
+    ok = mbar_wait_warp(&never[0], 0, &mine, sync, budget, suspend_hint_ns(budget));
   else
-    ok = mbar_wait_idle_warp(&never[1], 0, &mine, sync, budget);
+    ok = mbar_wait_idle_warp(&never[1], 0, &mine, sync, budget, suspend_hint_ns(budget));
   if (!ok && (threadIdx.x & 31) == 0) atomicAdd(&abort_flag, 1);
   __syncthreads();
   if (threadIdx.x == 0 && abort_flag != 2) record_error(sync, PB2_ERR_INVALID_ARGUMENT);

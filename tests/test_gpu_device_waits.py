@@ -61,11 +61,13 @@ def test_wait_selftest_rejects_bad_budget():
 
 
 def test_mined_gemm_unwinds_when_its_waits_run_out():
-    """With a 64-cycle budget the MMA issuer gives up on its first operand
-    stage (a TMA load takes far longer): the abort reaches every role, the
-    producer drains its loads, the MMA warp retires what it issued, TMEM is
-    released, and the kernel returns with the timeout recorded."""
-    m, n, k, r = 512, 512, 1024, 128
+    """With a 64-cycle budget a wait gives up: the abort reaches every role,
+    the producer drains its loads, the MMA warp retires what it issued, TMEM
+    is released, and the kernel returns with the timeout recorded.  A wait's
+    first try_wait may sleep for a system-defined time before the budget is
+    looked at, so the problem is long enough (K = 8192: 64 chunks per tile)
+    that the hash warps' wait for a tile's transcripts outlasts it."""
+    m, n, k, r = 512, 512, 8192, 128
     p = make_problem(m, n, k, r, seed=73)
     gen_noise(p)
     _, sync = run_noisy_gemm(p, 0)  # noised operands and factors in place
